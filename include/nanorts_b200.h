@@ -1,0 +1,156 @@
+/*
+ * nanorts_b200: C ABI of the B200-native NanoRTS batched environment step.
+ *
+ * Every entry point takes plain device pointers (lane-major buffers, leading
+ * extent L = games), sizes and a CUDA stream passed as `void*`; none
+ * allocates, synchronises the host or keeps per-call state.  Calls are
+ * stream-ordered and asynchronous.  Each returns 0 on success or a negative
+ * NRTS_E_* code; nrts_last_error() then names the problem (per host thread).
+ *
+ * Buffers (per game; all lane-major [L, ...], C = per-player slot capacity,
+ * E = neutral + 2*C slots, H x W field):
+ *   State leaves (NrtsState.leaf, in the order of NrtsLeaf): the reference's
+ *     State pytree leaves (src/nanorts/model/state.py:27-84) with their dtypes;
+ *     cell/slot indices are int16.  Updated in place.
+ *   actions[p]       int32 [L, C, 7]    one row per player slot (factor order
+ *                                       kind, move/harvest/return/produce
+ *                                       direction, produce type, attack offset)
+ *   masks[p]         uint8 [L, C, 6+16+T+O]  0/1 legality rows
+ *   feature_maps[p]  uint8 [L, H, W, 6]
+ *   scalars[p]       int32 [L, 4]
+ *
+ * Reference interfaces replaced (paths under src/nanorts/ of NanoRTS):
+ *   nrts_step          XLA FFI targets nanorts_step (core/cuda/step.cu:653-698),
+ *                      nanorts_reset_packed_where_done (adapters/cuda/reset.cu:196),
+ *                      nanorts_legality_words (core/cuda/legality.cu:547-561) and
+ *                      nanorts_visible_cells (observations/cuda/visibility.cu) plus
+ *                      the XLA fusions of decode_actions, observe and mask
+ *                      assembly, as called by NanoRTS.step (adapters/jaxmarl/facade.py:107-119)
+ *   nrts_reset         NanoRTS.reset (adapters/jaxmarl/facade.py:100-105)
+ *   nrts_legal_masks   NanoRTS.get_avail_actions (facade.py:172-174 -> core/cuda/legality.cu)
+ *   nrts_observe       NanoRTS.get_obs (facade.py:166-170 -> observations/cuda/visibility.cu)
+ *   nrts_slot_cells    NanoRTS.get_slot_cells (facade.py:176-178)
+ *   nrts_build_id      nanorts_build_id (kernels/cuda/registry.cu:201-229)
+ *   nrts_self_check    nanorts_self_check (kernels/cuda/registry.cu:201-229)
+ */
+#ifndef NANORTS_B200_H
+#define NANORTS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum NrtsStatus {
+    NRTS_OK = 0,
+    NRTS_E_ARGUMENT = -1,    /* a null pointer, a bad extent or an unsupported configuration */
+    NRTS_E_CUDA = -2,        /* a CUDA runtime error (launch or attribute) */
+    NRTS_E_DEVICE = -3,      /* the device reported an error in the status word */
+};
+
+/* State leaves, in the reference's declaration order (state.py:35-80); the
+ * same order as the reference step kernel's Leaf enum (core/cuda/step.cu:61-85). */
+enum NrtsLeaf {
+    NRTS_BIRTH, NRTS_UNIT_TYPE, NRTS_OWNER, NRTS_CELL, NRTS_HIT_POINTS, NRTS_CARRIED_RESOURCES,
+    NRTS_PENDING_KIND, NRTS_PENDING_DIRECTION, NRTS_PENDING_NONE_DURATION, NRTS_PENDING_TARGET_CELL,
+    NRTS_PENDING_PRODUCED_TYPE, NRTS_PENDING_ISSUED_AT, NRTS_PENDING_COMPLETES_AT, NRTS_PENDING_ORDER,
+    NRTS_ENTITY_AT, NRTS_TIME, NRTS_PLAYER_RESOURCES, NRTS_NEXT_BIRTH, NRTS_NEXT_PENDING_ORDER,
+    NRTS_ALTERNATING_CONFLICT_COUNT, NRTS_GAME_OVER, NRTS_WINNER, NRTS_SPAWN_OVERFLOW,
+    NRTS_LEAVES
+};
+
+/* Static extents of one scenario (BucketSpec, model/bucket.py:24-105). */
+typedef struct NrtsExtents {
+    int32_t height, width;        /* field; width <= 64 */
+    int32_t neutral;              /* neutral slots */
+    int32_t capacity;             /* slots per player (C) */
+    int32_t types;                /* unit types (T) */
+    int32_t offsets;              /* attack window cells (O = side^2, side <= 7) */
+    int32_t strategy;             /* 0 CANCEL_BOTH, 1 CANCEL_RANDOM, 2 CANCEL_ALTERNATING */
+    int32_t max_cycles;           /* time limit */
+    int32_t partial_observability;/* 0/1 */
+} NrtsExtents;
+
+/* Per-scenario constants, device pointers. */
+typedef struct NrtsContent {
+    const uint8_t* terrain;       /* [H*W] 0/1 walls */
+    const int32_t* table;         /* [T, 15+T] unit table: cost, hit_points, produce_time, move_time,
+                                     attack_time, harvest_time, attack_range, attack_damage,
+                                     harvest_amount, sight_radius, is_resource, is_stockpile,
+                                     can_harvest, can_move, can_attack, produces[T] */
+    const void* reset[NRTS_LEAVES]; /* one game's reset State, decide(initial_state) */
+} NrtsContent;
+
+/* A batch of games, device pointers, updated in place. */
+typedef struct NrtsState {
+    void* leaf[NRTS_LEAVES];
+    uint32_t* environment_root;   /* [L, 2] threefry key data of each game's reset key */
+    uint32_t* episode_index;      /* [L] */
+} NrtsState;
+
+/* Outputs of a step, device pointers.  Null pointers skip that output. */
+typedef struct NrtsOutputs {
+    uint8_t* masks[2];            /* legality rows of the carried (post-reset) state */
+    uint8_t* feature_maps[2];     /* observation of the carried state */
+    int32_t* scalars[2];
+    float* reward;                /* [L, 2] */
+    uint8_t* done;                /* [L] terminated | truncated */
+    uint8_t* terminated;          /* [L] */
+    uint8_t* truncated;           /* [L] */
+    int32_t* winner;              /* [L] of the ending state, before the reset */
+    int32_t* spawn_overflow;      /* [L, 2] telemetry of the ending state */
+    uint8_t* final_feature_maps[2]; /* observation of the ending state, before the reset */
+    int32_t* final_scalars[2];
+} NrtsOutputs;
+
+/* One environment step for every game: decode the action rows, the core step
+ * (admission, conflicts, completion, outcome), auto-reset of finished games,
+ * then the next step's masks and both players' observations.
+ * Replaces NanoRTS.step (adapters/jaxmarl/facade.py:107-119). */
+int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+              const int32_t* actions0, const int32_t* actions1, const NrtsOutputs* outputs, void* stream);
+
+/* Every game to its reset State with episode 0 and the given root keys
+ * ([L, 2] uint32, may alias state->environment_root); writes masks and
+ * observations of that state.  Replaces NanoRTS.reset (facade.py:100-105). */
+int nrts_reset(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+               const uint32_t* keys, const NrtsOutputs* outputs, void* stream);
+
+/* Legality rows of the current state (get_avail_actions, facade.py:172-174). */
+int nrts_legal_masks(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+                     uint8_t* masks0, uint8_t* masks1, void* stream);
+
+/* Observations of the current state (get_obs, facade.py:166-170). */
+int nrts_observe(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+                 uint8_t* feature_maps0, uint8_t* feature_maps1, int32_t* scalars0, int32_t* scalars1, void* stream);
+
+/* int32 [L, 2, C] cell of each player slot, -1 when empty (get_slot_cells, facade.py:176-178). */
+int nrts_slot_cells(const NrtsExtents* extents, const NrtsState* state, int64_t lanes, int32_t* cells, void* stream);
+
+/* Uniform draw over the set bits of each factor group of every mask row
+ * (0 when a group has none), for rollouts and benchmarks: the stand-in for
+ * per-factor jax.random.categorical over masked logits (README.md:53-63).
+ * Deterministic in (seed, counter, game, player, slot, factor). */
+int nrts_sample_actions(const NrtsExtents* extents, int64_t lanes, const uint8_t* masks0, const uint8_t* masks1,
+                        int32_t* actions0, int32_t* actions1, uint64_t seed, uint64_t counter, void* stream);
+
+/* Status word: the device writes a nonzero code here when a kernel's bounded
+ * wait gives up.  Reads it (synchronously), clears it and returns it. */
+int nrts_device_status(int device);
+
+/* Build identity string of this library. */
+const char* nrts_build_id(void);
+
+/* Runs a probe kernel on each listed device and checks warp ballot and
+ * shuffle results and that every kernel image loads.  Returns 0 when all pass. */
+int nrts_self_check(const int32_t* devices, int64_t count);
+
+/* Message of the last failed call on this host thread. */
+const char* nrts_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NANORTS_B200_H */

@@ -1,0 +1,413 @@
+"""The NanoRTS JaxMARL surface over the sm_100a kernels.
+
+Mirrors ``src/nanorts/adapters/jaxmarl/facade.py`` (``make`` and ``NanoRTS``
+with ``reset``, ``step``, ``get_avail_actions``, ``get_obs``,
+``get_slot_cells``, ``layout``) for a batch of games held in torch tensors on
+one CUDA device.  The reference environment is written per game and batched
+by ``jax.vmap``; this one is batched natively: every leaf has a leading lane
+axis ``L``, the same layout ``vmap`` gives the reference's pytrees.
+
+Differences a caller of the reference sees:
+  * keys are threefry key data, ``uint32[L, 2]`` tensors (``jax.random.key_data``
+    of the per-game keys);
+  * ``step`` updates the EnvironmentState in place (the reference's kernel
+    path aliases the state buffers too) and returns the same object;
+  * outputs of a call are views of per-state buffers that the next call on
+    that state overwrites; ``.clone()`` what must be kept.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+from typing import Any
+
+import numpy as np
+import torch
+
+from nanorts_b200 import content as _content
+from nanorts_b200.model import (
+    ACTION_KIND_COUNT,
+    DIRECTION_COUNT,
+    KIND_NONE,
+    PLAYER_COUNT,
+    STRATEGY_CODES,
+    GameConfig,
+    ModelError,
+    UnitTypeTableVersion,
+    leaf_shapes,
+)
+from nanorts_b200.runtime import Content, Extents, Outputs, StatePtrs, check, library
+
+AGENTS = tuple(f"player_{p}" for p in range(PLAYER_COUNT))
+ALL_AGENTS = "__all__"
+ENVIRONMENT_IDS = ("NanoRTS",)
+ACTION_FACTORS = ("kind", "move_direction", "harvest_direction", "return_direction", "produce_direction",
+                  "produce_type", "attack_offset")
+NONE_DURATION = 1
+
+LEAVES = (
+    "birth", "unit_type", "owner", "cell", "hit_points", "carried_resources", "pending_kind", "pending_direction",
+    "pending_none_duration", "pending_target_cell", "pending_produced_type", "pending_issued_at",
+    "pending_completes_at", "pending_order", "entity_at", "time", "player_resources", "next_birth",
+    "next_pending_order", "alternating_conflict_count", "game_over", "winner", "spawn_overflow",
+)
+
+_TORCH_DTYPES = {
+    np.dtype(np.int8): torch.int8, np.dtype(np.int16): torch.int16, np.dtype(np.int32): torch.int32,
+    np.dtype(np.bool_): torch.bool, np.dtype(np.uint8): torch.uint8,
+}
+
+
+@dataclasses.dataclass
+class Telemetry:
+    spawn_overflow: torch.Tensor
+
+
+@dataclasses.dataclass
+class State:
+    """Core State of L games, one tensor per reference leaf (model/state.py:35-80)."""
+
+    birth: torch.Tensor
+    unit_type: torch.Tensor
+    owner: torch.Tensor
+    cell: torch.Tensor
+    hit_points: torch.Tensor
+    carried_resources: torch.Tensor
+    pending_kind: torch.Tensor
+    pending_direction: torch.Tensor
+    pending_none_duration: torch.Tensor
+    pending_target_cell: torch.Tensor
+    pending_produced_type: torch.Tensor
+    pending_issued_at: torch.Tensor
+    pending_completes_at: torch.Tensor
+    pending_order: torch.Tensor
+    entity_at: torch.Tensor
+    time: torch.Tensor
+    player_resources: torch.Tensor
+    next_birth: torch.Tensor
+    next_pending_order: torch.Tensor
+    alternating_conflict_count: torch.Tensor
+    game_over: torch.Tensor
+    winner: torch.Tensor
+    spawn_overflow: torch.Tensor
+
+    @property
+    def active(self) -> torch.Tensor:
+        return self.birth != -1
+
+    @property
+    def telemetry(self) -> Telemetry:
+        return Telemetry(spawn_overflow=self.spawn_overflow)
+
+    def leaves(self) -> list[torch.Tensor]:
+        return [getattr(self, name) for name in LEAVES]
+
+
+@dataclasses.dataclass
+class SymbolicObservation:
+    feature_maps: torch.Tensor  # uint8 [L, H, W, 6]
+    scalars: torch.Tensor       # int32 [L, 4]
+
+
+@dataclasses.dataclass
+class EnvironmentState:
+    """lifecycle.EnvironmentState (adapters/lifecycle.py:24-31) over L lanes."""
+
+    core_state: State
+    environment_root: torch.Tensor  # uint32 [L, 2]
+    episode_index: torch.Tensor     # uint32 [L]
+    _buffers: dict[str, torch.Tensor] = dataclasses.field(default_factory=dict, repr=False)
+    _masks_current: bool = dataclasses.field(default=False, repr=False)
+
+    @property
+    def lanes(self) -> int:
+        return int(self.episode_index.shape[0])
+
+
+@dataclasses.dataclass(frozen=True)
+class JaxMARLLayout:
+    """adapters/jaxmarl/layout.py:34-67."""
+
+    height: int
+    width: int
+    per_player_capacity: int
+    surface: str
+    partial_observability: bool
+    final_observation: bool
+    action_widths: tuple[int, ...]
+    mask_offsets: tuple[int, ...]
+    mask_width: int
+    feature_maps_dtype: torch.dtype
+
+    @property
+    def agents(self) -> tuple[str, ...]:
+        return AGENTS
+
+    @property
+    def action_factors(self) -> tuple[str, ...]:
+        return ACTION_FACTORS
+
+    @property
+    def actions_shape(self) -> tuple[int, int]:
+        return (self.per_player_capacity, len(ACTION_FACTORS))
+
+    @property
+    def mask_shape(self) -> tuple[int, int]:
+        return (self.per_player_capacity, self.mask_width)
+
+
+def make(env_id: str, *, scenario: GameConfig, utt: UnitTypeTableVersion | None = None, surface: str = "symbolic",
+         partial_observability: bool = False, final_observation: bool = True, feature_dtype: Any = None,
+         reward_components: bool = False, device: Any = None) -> NanoRTS:
+    """``nanorts.make`` (adapters/jaxmarl/facade.py:43-56)."""
+    if env_id not in ENVIRONMENT_IDS:
+        raise ModelError(f"make refuses environment id {env_id!r}: the accepted ids are {list(ENVIRONMENT_IDS)}")
+    game = scenario if utt is None else _content.with_unit_type_table(scenario, utt)
+    return NanoRTS(game, surface=surface, partial_observability=partial_observability,
+                   final_observation=final_observation, feature_dtype=feature_dtype,
+                   reward_components=reward_components, device=device)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    if t is None:
+        return None
+    assert t.is_contiguous()
+    return t.data_ptr()
+
+
+class NanoRTS:
+    """The two-player environment over batches of games on one CUDA device."""
+
+    def __init__(self, scenario: GameConfig, *, surface: str = "symbolic", partial_observability: bool = False,
+                 final_observation: bool = True, feature_dtype: Any = None, reward_components: bool = False,
+                 device: Any = None) -> None:
+        if surface != "symbolic":
+            raise ModelError(f"NanoRTS refuses surface={surface!r}: this build publishes the symbolic surface only")
+        if not isinstance(partial_observability, bool) or not isinstance(final_observation, bool):
+            raise ModelError("partial_observability and final_observation must be bools")
+        if reward_components:
+            raise ModelError("NanoRTS refuses reward_components=True: the shaped reward components are not built here")
+        if feature_dtype is None:
+            feature_dtype = torch.uint8
+        if feature_dtype not in (torch.uint8, torch.int16, torch.int32):
+            raise ModelError(f"feature_dtype {feature_dtype!r} is none of uint8, int16, int32")
+        bucket = scenario.bucket
+        if bucket.index_dtype != np.int16:
+            raise ModelError("this build steps scenarios whose cell and slot indices fit int16")
+        if bucket.width > 64 or bucket.height > 64:
+            raise ModelError(f"this build steps fields up to 64x64, not {bucket.height}x{bucket.width}")
+        reset = _content.decide(scenario.initial_state, bucket)
+        if bool(reset["game_over"]):
+            raise ModelError("NanoRTS refuses a scenario whose initial State is already decided")
+        self.game = scenario
+        self.agents = list(AGENTS)
+        self.num_agents = PLAYER_COUNT
+        self.final_observation = final_observation
+        self.partial_observability = partial_observability
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        widths = (ACTION_KIND_COUNT, DIRECTION_COUNT, DIRECTION_COUNT, DIRECTION_COUNT, DIRECTION_COUNT,
+                  bucket.unit_type_capacity, bucket.attack_offset_capacity)
+        offsets = tuple(int(v) for v in np.cumsum((0, *widths[:-1])))
+        self.layout = JaxMARLLayout(
+            height=bucket.height, width=bucket.width, per_player_capacity=bucket.per_player_capacity,
+            surface=surface, partial_observability=partial_observability, final_observation=final_observation,
+            action_widths=widths, mask_offsets=offsets, mask_width=sum(widths), feature_maps_dtype=feature_dtype,
+        )
+        self._shapes = leaf_shapes(bucket)
+        self._extents = Extents(
+            height=bucket.height, width=bucket.width, neutral=bucket.neutral_capacity,
+            capacity=bucket.per_player_capacity, types=bucket.unit_type_capacity,
+            offsets=bucket.attack_offset_capacity, strategy=STRATEGY_CODES[bucket.conflict_strategy],
+            max_cycles=scenario.max_cycles, partial_observability=int(partial_observability),
+        )
+        self._terrain = torch.from_numpy(scenario.terrain.reshape(-1).astype(np.uint8)).to(self.device)
+        self._table = torch.from_numpy(scenario.table).to(self.device)
+        self._reset_rows = {
+            name: torch.from_numpy(np.ascontiguousarray(reset[name]).astype(self._shapes[name][1])).to(self.device)
+            for name in LEAVES
+        }
+        self._content = Content(terrain=_ptr(self._terrain), table=_ptr(self._table))
+        for k, name in enumerate(LEAVES):
+            self._content.reset[k] = _ptr(self._reset_rows[name])
+        library()  # fail loudly now when the kernels are missing
+
+    # -- buffers ----------------------------------------------------------------
+    def _empty_state(self, lanes: int) -> EnvironmentState:
+        leaves = {}
+        for name in LEAVES:
+            shape, dtype, _ = self._shapes[name]
+            leaves[name] = torch.empty((lanes, *shape), dtype=_TORCH_DTYPES[np.dtype(dtype)], device=self.device)
+        return EnvironmentState(
+            core_state=State(**leaves),
+            environment_root=torch.empty((lanes, 2), dtype=torch.uint32, device=self.device),
+            episode_index=torch.empty((lanes,), dtype=torch.uint32, device=self.device),
+        )
+
+    def _buffers(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
+        if state._buffers:
+            return state._buffers
+        L, b, dev = state.lanes, self.game.bucket, self.device
+        u8 = torch.uint8
+        buf = {
+            "masks": torch.empty((PLAYER_COUNT, L, b.per_player_capacity, self.layout.mask_width), dtype=u8, device=dev),
+            "feature_maps": torch.empty((PLAYER_COUNT, L, b.height, b.width, 6), dtype=u8, device=dev),
+            "scalars": torch.empty((PLAYER_COUNT, L, 4), dtype=torch.int32, device=dev),
+            "reward": torch.empty((L, PLAYER_COUNT), dtype=torch.float32, device=dev),
+            "done": torch.empty((L,), dtype=u8, device=dev),
+            "terminated": torch.empty((L,), dtype=u8, device=dev),
+            "truncated": torch.empty((L,), dtype=u8, device=dev),
+            "winner": torch.empty((L,), dtype=torch.int32, device=dev),
+            "spawn_overflow": torch.empty((L, PLAYER_COUNT), dtype=torch.int32, device=dev),
+        }
+        if self.final_observation:
+            buf["final_feature_maps"] = torch.empty_like(buf["feature_maps"])
+            buf["final_scalars"] = torch.empty_like(buf["scalars"])
+        state._buffers = buf
+        return buf
+
+    def _state_ptrs(self, state: EnvironmentState) -> StatePtrs:
+        ptrs = StatePtrs(environment_root=_ptr(state.environment_root), episode_index=_ptr(state.episode_index))
+        for k, leaf in enumerate(state.core_state.leaves()):
+            if leaf.device != self.device or not leaf.is_contiguous():
+                raise ModelError("every state leaf must be a contiguous tensor on the environment's device")
+            ptrs.leaf[k] = leaf.data_ptr()
+        return ptrs
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _observations(self, buf: dict[str, torch.Tensor], prefix: str = "") -> dict[str, SymbolicObservation]:
+        maps, scalars = buf[prefix + "feature_maps"], buf[prefix + "scalars"]
+        dtype = self.layout.feature_maps_dtype
+        return {
+            agent: SymbolicObservation(
+                feature_maps=maps[p] if dtype == torch.uint8 else maps[p].to(dtype),
+                scalars=scalars[p],
+            )
+            for p, agent in enumerate(self.agents)
+        }
+
+    # -- the JaxMARL surface ----------------------------------------------------
+    def reset(self, key: torch.Tensor) -> tuple[dict[str, SymbolicObservation], EnvironmentState]:
+        """env.reset over lanes: ``key`` is uint32[L, 2] threefry key data (facade.py:100-105)."""
+        key = torch.as_tensor(key)
+        if key.ndim != 2 or key.shape[1] != 2:
+            raise ModelError(f"reset keys have shape {tuple(key.shape)}, expected [L, 2] key data")
+        key = key.to(device=self.device, dtype=torch.uint32).contiguous()
+        state = self._empty_state(int(key.shape[0]))
+        buf = self._buffers(state)
+        out = Outputs()
+        out.masks[0], out.masks[1] = _ptr(buf["masks"][0]), _ptr(buf["masks"][1])
+        out.feature_maps[0], out.feature_maps[1] = _ptr(buf["feature_maps"][0]), _ptr(buf["feature_maps"][1])
+        out.scalars[0], out.scalars[1] = _ptr(buf["scalars"][0]), _ptr(buf["scalars"][1])
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_reset(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs),
+                                   state.lanes, _ptr(key), ctypes.byref(out), self._stream()))
+        state._masks_current = True
+        return self._observations(buf), state
+
+    def step(self, key: Any, state: EnvironmentState, actions: dict[str, torch.Tensor],
+             reset_state: Any = None) -> tuple[dict[str, SymbolicObservation], EnvironmentState, dict, dict, dict]:
+        """env.step (facade.py:107-119): the key is ignored, as in the reference."""
+        del key
+        if reset_state is not None:
+            raise ModelError("NanoRTS.step refuses a reset_state: auto-reset restarts each game at its own root")
+        buf = self._buffers(state)
+        L, C = state.lanes, self.game.bucket.per_player_capacity
+        rows = []
+        for agent in self.agents:
+            a = actions[agent]
+            if a.shape != (L, C, 7) or a.dtype != torch.int32 or a.device != self.device or not a.is_contiguous():
+                raise ModelError(f"actions[{agent!r}] must be a contiguous int32 tensor [L, {C}, 7] on {self.device}")
+            rows.append(a)
+        out = Outputs()
+        for p in range(PLAYER_COUNT):
+            out.masks[p] = _ptr(buf["masks"][p])
+            out.feature_maps[p] = _ptr(buf["feature_maps"][p])
+            out.scalars[p] = _ptr(buf["scalars"][p])
+            if self.final_observation:
+                out.final_feature_maps[p] = _ptr(buf["final_feature_maps"][p])
+                out.final_scalars[p] = _ptr(buf["final_scalars"][p])
+        for name in ("reward", "done", "terminated", "truncated", "winner", "spawn_overflow"):
+            setattr(out, name, _ptr(buf[name]))
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_step(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs), L,
+                                  _ptr(rows[0]), _ptr(rows[1]), ctypes.byref(out), self._stream()))
+        state._masks_current = True
+        done = buf["done"].view(torch.bool)
+        rewards = {agent: buf["reward"][:, p] for p, agent in enumerate(self.agents)}
+        dones = {agent: done for agent in self.agents} | {ALL_AGENTS: done}
+        infos: dict[str, Any] = {
+            "terminated": buf["terminated"].view(torch.bool),
+            "truncated": buf["truncated"].view(torch.bool),
+            "winner": buf["winner"],
+            "telemetry": Telemetry(spawn_overflow=buf["spawn_overflow"]),
+            "spawn_overflowed": (buf["spawn_overflow"] > 0).any(dim=1),
+            "final_valid": done,
+        }
+        if self.final_observation:
+            infos["final_observation"] = self._observations(buf, "final_")
+        return self._observations(buf), state, rewards, dones, infos
+
+    def get_avail_actions(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
+        """bool[L, C, 78] per agent (facade.py:172-174); reuses the rows the last step wrote."""
+        buf = self._buffers(state)
+        if not state._masks_current:
+            ptrs = self._state_ptrs(state)
+            check(library().nrts_legal_masks(ctypes.byref(self._extents), ctypes.byref(self._content),
+                                             ctypes.byref(ptrs), state.lanes, _ptr(buf["masks"][0]),
+                                             _ptr(buf["masks"][1]), self._stream()))
+            state._masks_current = True
+        return {agent: buf["masks"][p].view(torch.bool) for p, agent in enumerate(self.agents)}
+
+    def invalidate(self, state: EnvironmentState) -> None:
+        """Marks cached masks stale after the caller edited the state's leaves."""
+        state._masks_current = False
+
+    def get_obs(self, state: EnvironmentState) -> dict[str, SymbolicObservation]:
+        """facade.py:166-170."""
+        buf = self._buffers(state)
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_observe(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs),
+                                     state.lanes, _ptr(buf["feature_maps"][0]), _ptr(buf["feature_maps"][1]),
+                                     _ptr(buf["scalars"][0]), _ptr(buf["scalars"][1]), self._stream()))
+        return self._observations(buf)
+
+    def get_slot_cells(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
+        """int32[L, C] per agent, -1 for an empty slot (facade.py:176-178)."""
+        L, C = state.lanes, self.game.bucket.per_player_capacity
+        cells = torch.empty((L, PLAYER_COUNT, C), dtype=torch.int32, device=self.device)
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_slot_cells(ctypes.byref(self._extents), ctypes.byref(ptrs), L, _ptr(cells), self._stream()))
+        return {agent: cells[:, p] for p, agent in enumerate(self.agents)}
+
+    def sample_actions(self, state: EnvironmentState, seed: int, counter: int) -> dict[str, torch.Tensor]:
+        """Uniform legal actions per factor from the current masks (the rollout stand-in for
+        per-factor categorical sampling over masked logits, README.md:53-63)."""
+        masks = self.get_avail_actions(state)
+        buf = self._buffers(state)
+        if "actions" not in buf:
+            buf["actions"] = torch.empty((PLAYER_COUNT, state.lanes, self.game.bucket.per_player_capacity, 7),
+                                         dtype=torch.int32, device=self.device)
+        acts = buf["actions"]
+        check(library().nrts_sample_actions(ctypes.byref(self._extents), state.lanes, _ptr(masks["player_0"]),
+                                            _ptr(masks["player_1"]), _ptr(acts[0]), _ptr(acts[1]),
+                                            seed & (2**64 - 1), counter & (2**64 - 1), self._stream()))
+        return {agent: acts[p] for p, agent in enumerate(self.agents)}
+
+    def observation_space(self, agent: str) -> dict[str, Any]:
+        return {"feature_maps": ((self.layout.height, self.layout.width, 6), self.layout.feature_maps_dtype),
+                "scalars": ((4,), torch.int32)}
+
+    def action_space(self, agent: str) -> dict[str, Any]:
+        return {"shape": self.layout.actions_shape, "high": tuple(w - 1 for w in self.layout.action_widths)}
+
+    @property
+    def agent_classes(self) -> dict[str, list[str]]:
+        return {"player": list(self.agents)}
+
+    def idle_row(self) -> torch.Tensor:
+        row = torch.zeros(self.layout.mask_width, dtype=torch.bool)
+        row[self.layout.mask_offsets[0] + KIND_NONE] = True
+        return row

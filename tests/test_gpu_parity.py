@@ -1,0 +1,127 @@
+"""Kernel vs oracle, bit for bit, at every step (needs a B200).
+
+Every State leaf, both players' legality rows, feature maps and scalars,
+rewards, dones, winners and telemetry of the sm_100a path are compared with
+the CPU oracle's on the same seeded action stream, including episodes that
+end and auto-reset inside the run (short horizons force truncation).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from tests.parity import CONFIGS, random_keys, sample
+
+pytestmark = pytest.mark.gpu
+
+LEAVES = (
+    "birth", "unit_type", "owner", "cell", "hit_points", "carried_resources", "pending_kind", "pending_direction",
+    "pending_none_duration", "pending_target_cell", "pending_produced_type", "pending_issued_at",
+    "pending_completes_at", "pending_order", "entity_at", "time", "player_resources", "next_birth",
+    "next_pending_order", "alternating_conflict_count", "game_over", "winner", "spawn_overflow",
+)
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.uint32:
+        t = t.view(torch.int32)
+    return t.cpu().numpy()
+
+
+def compare_state(env_state, orc, where: str) -> None:
+    core = env_state.core_state
+    for name in LEAVES:
+        got = _np(getattr(core, name))
+        want = orc.state[name]
+        if got.dtype == np.bool_:
+            want = want.astype(bool)
+        if not np.array_equal(got, want.reshape(got.shape)):
+            bad = np.argwhere(got != want.reshape(got.shape))[:5]
+            raise AssertionError(f"{where}: leaf {name} differs at {bad.tolist()}")
+    assert np.array_equal(_np(env_state.episode_index).astype(np.uint32), orc.episode_index), f"{where}: episode_index"
+    assert np.array_equal(_np(env_state.environment_root).astype(np.uint32), orc.environment_root), f"{where}: root"
+
+
+def compare_obs(obs, want, where: str, prefix: str = "") -> None:
+    for p, agent in enumerate(("player_0", "player_1")):
+        fm = _np(obs[agent].feature_maps)
+        sc = _np(obs[agent].scalars)
+        wf, ws = want[prefix + "feature_maps"][:, p], want[prefix + "scalars"][:, p]
+        if not np.array_equal(fm, wf):
+            bad = np.argwhere(fm != wf)[:5]
+            raise AssertionError(f"{where}: {prefix}feature_maps of {agent} differ at {bad.tolist()}")
+        assert np.array_equal(sc, ws), f"{where}: {prefix}scalars of {agent}"
+
+
+def compare_masks(env, env_state, orc, where: str) -> np.ndarray:
+    masks = env.get_avail_actions(env_state)
+    want = orc.legal_masks()
+    for p, agent in enumerate(("player_0", "player_1")):
+        got = _np(masks[agent]).astype(np.uint8)
+        if not np.array_equal(got, want[:, p]):
+            bad = np.argwhere(got != want[:, p])[:5]
+            raise AssertionError(f"{where}: masks of {agent} differ at {bad.tolist()}")
+    return want
+
+
+def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycles: int | None = None,
+               move_bias: float = 0.0, final_observation: bool = True) -> dict:
+    from nanorts_b200.env import make
+    from oracle.oracle import Oracle
+
+    cfg = CONFIGS[config_name]
+    game = cfg.game(max_cycles)
+    env = make("NanoRTS", scenario=game, partial_observability=cfg.partial, final_observation=final_observation)
+    orc = Oracle(game, lanes, partial_observability=cfg.partial, final_observation=final_observation)
+    rng = np.random.default_rng(seed)
+    keys = random_keys(rng, lanes)
+    obs, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
+    want_obs = orc.reset(keys)
+    compare_state(state, orc, "reset")
+    compare_obs(obs, want_obs, "reset")
+    episodes = 0
+    for t in range(steps):
+        masks = compare_masks(env, state, orc, f"step {t} masks")
+        actions = sample(masks, rng, move_bias)
+        want = orc.step(actions)
+        acts = {f"player_{p}": torch.from_numpy(np.ascontiguousarray(actions[:, p])).cuda() for p in range(2)}
+        obs, state, rewards, dones, infos = env.step(None, state, acts)
+        where = f"{config_name} step {t}"
+        compare_state(state, orc, where)
+        compare_obs(obs, want, where)
+        if final_observation:
+            compare_obs(infos["final_observation"], want, where, prefix="final_")
+        for p in range(2):
+            assert np.array_equal(_np(rewards[f"player_{p}"]), want["reward"][:, p]), f"{where}: reward {p}"
+        assert np.array_equal(_np(dones["__all__"]), want["done"]), f"{where}: done"
+        assert np.array_equal(_np(infos["terminated"]), want["terminated"]), f"{where}: terminated"
+        assert np.array_equal(_np(infos["truncated"]), want["truncated"]), f"{where}: truncated"
+        assert np.array_equal(_np(infos["winner"]), want["winner"]), f"{where}: winner"
+        assert np.array_equal(_np(infos["telemetry"].spawn_overflow), want["spawn_overflow"]), f"{where}: overflow"
+        episodes += int(want["done"].sum())
+    return {"episodes": episodes, "time": orc.state["time"].copy(), "alt": orc.state["alternating_conflict_count"].copy()}
+
+
+@pytest.mark.parametrize("config_name", ["c1_8x8_both", "c2_16x16_random", "c3_16x16_alternating_partial"])
+def test_parity_small_boards(config_name):
+    stats = run_parity(config_name, lanes=96, steps=400, seed=1, max_cycles=150)
+    assert stats["episodes"] > 0  # auto-reset exercised
+
+
+@pytest.mark.parametrize("config_name", ["c2_16x16_random", "c3_16x16_alternating_partial", "c1_8x8_both"])
+def test_parity_contested_moves(config_name):
+    """Move-biased play: many same-cycle and cross-cycle claim conflicts."""
+    stats = run_parity(config_name, lanes=64, steps=300, seed=7, move_bias=0.7, max_cycles=120)
+    if config_name.startswith("c3"):
+        assert stats["alt"].max() > 0  # CANCEL_ALTERNATING counted conflicts
+
+
+def test_parity_garden_of_war():
+    run_parity("c5_64x64_random", lanes=12, steps=200, seed=3, max_cycles=90)
+
+
+def test_parity_long_horizon():
+    """Games that run long enough for units to fight and die (default horizon)."""
+    run_parity("c2_16x16_random", lanes=48, steps=1200, seed=11, final_observation=False)
