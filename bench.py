@@ -1,0 +1,386 @@
+"""Benchmark: NanoRTS env-steps/s on B200 (BASELINE.json metric).
+
+Workload (configs[1] of BASELINE.json): basesWorkers16x16, VERSION_ORIGINAL,
+CANCEL_RANDOM, 70 slots per player, symbolic uint8[16,16,6] observations,
+16384 games per GPU, both players draw uniform random legal actions per
+factor from the masks, auto-reset.  One step = sample actions from the
+current masks (nrts_sample_actions) + one environment step of every game
+(nrts_step: decode, core step, auto-reset, next masks, both observations).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--lanes L] [--impl reference]
+
+Under torchrun each rank steps its own L games (weak scaling, no collective
+on the step path); one NCCL all-reduce of episode statistics runs after the
+timed region.  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "env steps/sec (both players, incl. masks+obs)"
+MAP, UTT, STRATEGY = "basesWorkers16x16", "VERSION_ORIGINAL", "CANCEL_RANDOM"
+DEFAULT_LANES = 16384
+
+
+def scenario():
+    from nanorts_b200 import map_name_to_scenario
+
+    return map_name_to_scenario(MAP, utt=UTT, conflict_strategy=STRATEGY, max_cycles=5000)
+
+
+def algorithmic_bytes(game) -> dict[str, int]:
+    """Bytes one env-step must move: the State read and written in place
+    (reference layout, with the 12 lifecycle bytes), both players' action
+    rows, legality rows, feature maps and scalars, and the step outputs."""
+    b = game.bucket
+    E, HW, C = b.entity_capacity, b.cell_count, b.per_player_capacity
+    state = 35 * E + 2 * HW + 37 + 12
+    parts = {
+        "state_read": state,
+        "state_write": state,
+        "actions": 2 * C * 7 * 4,
+        "masks": 2 * C * b.mask_width,
+        "observations": 2 * (HW * 6 + 16),
+        "outputs": 8 + 1 + 1 + 1 + 4 + 8,
+    }
+    parts["total"] = sum(parts.values())
+    return parts
+
+
+def load_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic() -> float | None:
+    """DRAM bytes per env-step of the step kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "step_kernel_16x16_traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("dram_bytes_per_env_step:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons through NVML while running."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unknown
+            self._nvml = None
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                mhz = self._nvml.nvmlDeviceGetClockInfo(self._handle, self._nvml.NVML_CLOCK_SM)
+                reasons = self._nvml.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._nvml is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        return {
+            "sm_mhz": statistics.median(m for m, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(name for name, bit in self.REASONS.items() if seen & bit),
+            "samples": len(self.samples),
+        }
+
+
+def cpu_baseline(game, seconds: float = 12.0, lanes: int = 512, threads: int | None = None) -> dict:
+    """The CPU oracle (C++ restatement of the reference's JAX program path,
+    OpenMP over games) on a bounded sample of the same workload."""
+    from oracle.oracle import Oracle, sample_uniform_legal
+
+    threads = threads or os.cpu_count() or 1
+    orc = Oracle(game, lanes, threads=threads)
+    rng = np.random.default_rng(0)
+    orc.reset(rng.integers(0, 2**32, size=(lanes, 2), dtype=np.uint64).astype(np.uint32))
+    widths = (6, 4, 4, 4, 4, game.bucket.unit_type_capacity, game.bucket.attack_offset_capacity)
+    for _ in range(3):  # warm-up
+        orc.step(sample_uniform_legal(orc.legal_masks(), widths, rng))
+    steps, step_time = 0, 0.0
+    start = time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        actions = sample_uniform_legal(orc.legal_masks(), widths, rng)
+        t0 = time.perf_counter()
+        orc.step(actions)
+        orc.legal_masks()  # masks of the next step are part of the metric
+        step_time += time.perf_counter() - t0
+        steps += 1
+    return {
+        "value": lanes * steps / step_time,
+        "unit": "env-steps/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{lanes} games x {steps} steps of {MAP}/{STRATEGY}, C++ oracle step + masks + observations "
+                  f"(sampling excluded), {threads} OpenMP threads",
+    }
+
+
+def run_reference(args) -> None:
+    """--impl reference: the reference's CPU path for this workload.  The reference
+    (JAX) cannot be installed here, so this times the C++ oracle port of its JAX
+    program on the host cores; each step is a bounded sample of the workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    game = scenario()
+    from oracle.oracle import Oracle, sample_uniform_legal
+
+    threads = os.cpu_count() or 1
+    lanes = 256
+    orc = Oracle(game, lanes, threads=threads)
+    rng = np.random.default_rng(0)
+    orc.reset(rng.integers(0, 2**32, size=(lanes, 2), dtype=np.uint64).astype(np.uint32))
+    widths = (6, 4, 4, 4, 4, game.bucket.unit_type_capacity, game.bucket.attack_offset_capacity)
+    for _ in range(args.warmup):
+        orc.step(sample_uniform_legal(orc.legal_masks(), widths, rng))
+    elapsed = 0.0
+    for _ in range(args.steps):
+        masks = orc.legal_masks()
+        actions = sample_uniform_legal(masks, widths, rng)
+        t0 = time.perf_counter()
+        orc.step(actions)
+        orc.legal_masks()
+        elapsed += time.perf_counter() - t0
+    value = lanes * args.steps / elapsed
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+        "config": {"workload": f"{MAP} {UTT} {STRATEGY}, uniform legal actions, auto-reset",
+                   "lanes_per_step_sample": lanes, "full_lanes": args.lanes},
+        "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
+                         "sample": f"{lanes} games per step on {threads} threads; the reference's JAX CPU path is not "
+                                   "runnable here (jax absent, reference install failed), so its C++ restatement runs"},
+        "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=2000)
+    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--lanes", type=int, default=DEFAULT_LANES, help="games per GPU")
+    parser.add_argument("--impl", default="nanorts_b200", choices=("nanorts_b200", "reference"))
+    parser.add_argument("--e2e-steps", type=int, default=50)
+    parser.add_argument("--stat-steps", type=int, default=200)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from nanorts_b200.env import make
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    game = scenario()
+    env = make("NanoRTS", scenario=game, final_observation=False, device=device)
+    L = args.lanes
+    rng = np.random.default_rng(1234 + rank)
+    keys = torch.from_numpy(rng.integers(0, 2**32, size=(L, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
+    _, state = env.reset(keys.to(device).view(torch.uint32))
+    stream = torch.cuda.current_stream(device)
+
+    def one_step(counter: int):
+        actions = env.sample_actions(state, seed=rank, counter=counter)
+        return env.step(None, state, actions)
+
+    for i in range(args.warmup):
+        one_step(i)
+    torch.cuda.synchronize(device)
+
+    # Timed region: K steps, events around every step kernel for the roofline.
+    done_total = torch.zeros((), dtype=torch.int64, device=device)
+    wins = torch.zeros(2, dtype=torch.int64, device=device)
+    step_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            actions = env.sample_actions(state, seed=rank, counter=args.warmup + i)
+            step_events[i][0].record(stream)
+            _, _, rewards, dones, infos = env.step(None, state, actions)
+            step_events[i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    elapsed_ms = start.elapsed_time(end)
+    step_kernel_ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+
+    # Episode statistics over a further untimed stretch, reduced once over NCCL.
+    for i in range(args.stat_steps):
+        _, _, rewards, dones, infos = one_step(10**9 + i)
+        done_total += dones["__all__"].sum()
+        wins += torch.stack([(infos["winner"] == p).logical_and(dones["__all__"]).sum() for p in range(2)])
+    stats = torch.cat([done_total.view(1), wins])
+    timing = torch.tensor([elapsed_ms, step_kernel_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.SUM)
+        dist.all_reduce(timing, op=dist.ReduceOp.MAX)
+    elapsed_ms, step_kernel_ms = timing.tolist()
+
+    # End to end through the public API with host buffers: each step copies the
+    # actions from pinned host memory, steps, samples the next actions on the
+    # device and reads the actions, rewards and dones back to the host.
+    C = game.bucket.per_player_capacity
+    host_actions = torch.empty((2, L, C, 7), dtype=torch.int32).pin_memory()
+    host_actions.copy_(torch.stack([a.cpu() for a in env.sample_actions(state, rank, 1).values()]))
+    host_rewards = torch.empty((L, 2), dtype=torch.float32).pin_memory()
+    host_dones = torch.empty((L,), dtype=torch.bool).pin_memory()
+    dev_actions = torch.empty((2, L, C, 7), dtype=torch.int32, device=device)
+    e2e_steps = args.e2e_steps
+
+    def e2e_step(i: int) -> None:
+        dev_actions.copy_(host_actions, non_blocking=True)
+        _, _, rewards, dones, _ = env.step(None, state, {"player_0": dev_actions[0], "player_1": dev_actions[1]})
+        nxt = env.sample_actions(state, seed=rank, counter=2 * 10**9 + i)
+        host_actions[0].copy_(nxt["player_0"], non_blocking=True)
+        host_actions[1].copy_(nxt["player_1"], non_blocking=True)
+        host_rewards.copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
+        host_dones.copy_(dones["__all__"], non_blocking=True)
+        stream.synchronize()
+
+    for i in range(3):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(3 + i)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    bytes_per = algorithmic_bytes(game)
+    peak, peak_kind = load_peaks()
+    achieved = bytes_per["total"] * L / (step_kernel_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+    line = None
+    if rank == 0:
+        value = world * L * args.steps / (elapsed_ms * 1e-3)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "env-steps/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"{MAP} {UTT} {STRATEGY}, C=70, uniform random legal actions per factor, auto-reset",
+                "games_per_gpu": L,
+                "global_games": world * L,
+                "parallelism": f"dp{world} (independent games per GPU)",
+                "step": "nrts_sample_actions + nrts_step",
+                "l2": "inputs larger than L2 (per-GPU working set "
+                      f"{(bytes_per['total'] + 2 * C * 7 * 4) * L / 1e6:.0f} MB)",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": traffic,
+                "kernel": "nrts::step_kernel",
+                "kernel_ms": step_kernel_ms,
+                "bytes_per_env_step": bytes_per["total"],
+                "peak_kind": peak_kind,
+            },
+            "clocks": clocks.summary(),
+            "e2e": {
+                "value": world * L * e2e_steps / (e2e_ms * 1e-3),
+                "unit": "env-steps/s",
+                "h2d_bytes_per_step": world * L * C * 7 * 4 * 2,
+                "d2h_bytes_per_step": world * (L * C * 7 * 4 * 2 + L * 2 * 4 + L),
+            },
+            "gpu_launches": 2 * args.steps,
+            "episodes": {"steps": args.stat_steps, "finished": int(stats[0]), "wins_p0": int(stats[1]),
+                         "wins_p1": int(stats[2])},
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(game)
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
