@@ -214,6 +214,8 @@ def main() -> None:
     parser.add_argument("--impl", default="nanorts_b200", choices=("nanorts_b200", "reference"))
     parser.add_argument("--e2e-steps", type=int, default=50)
     parser.add_argument("--stat-steps", type=int, default=200)
+    parser.add_argument("--separate-sampler", action="store_true",
+                        help="draw actions with nrts_sample_actions instead of inside nrts_step")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:
@@ -245,7 +247,14 @@ def main() -> None:
     _, state = env.reset(keys.to(device).view(torch.uint32))
     stream = torch.cuda.current_stream(device)
 
+    fused = not args.separate_sampler
+    current = {"actions": env.sample_actions(state, seed=rank, counter=0)}
+
     def one_step(counter: int):
+        if fused:  # draw the next actions inside the step kernel
+            out = env.step(None, state, current["actions"], sample=(rank, counter))
+            current["actions"] = out[4]["sampled_actions"]
+            return out
         actions = env.sample_actions(state, seed=rank, counter=counter)
         return env.step(None, state, actions)
 
@@ -264,10 +273,16 @@ def main() -> None:
     with ClockSampler(local) as clocks:
         start.record(stream)
         for i in range(args.steps):
-            actions = env.sample_actions(state, seed=rank, counter=args.warmup + i)
-            step_events[i][0].record(stream)
-            _, _, rewards, dones, infos = env.step(None, state, actions)
-            step_events[i][1].record(stream)
+            if fused:
+                step_events[i][0].record(stream)
+                out = env.step(None, state, current["actions"], sample=(rank, args.warmup + i))
+                current["actions"] = out[4]["sampled_actions"]
+                step_events[i][1].record(stream)
+            else:
+                actions = env.sample_actions(state, seed=rank, counter=args.warmup + i)
+                step_events[i][0].record(stream)
+                env.step(None, state, actions)
+                step_events[i][1].record(stream)
         end.record(stream)
         torch.cuda.synchronize(device)
     elapsed_ms = start.elapsed_time(end)
@@ -323,6 +338,9 @@ def main() -> None:
     e2e_ms = float(e2e_ms.item())
 
     bytes_per = algorithmic_bytes(game)
+    if fused:  # the step kernel also writes the drawn actions of the next step
+        bytes_per["sampled_actions"] = 2 * C * 7 * 4
+        bytes_per["total"] += bytes_per["sampled_actions"]
     peak, peak_kind = load_peaks()
     achieved = bytes_per["total"] * L / (step_kernel_ms * 1e-3) / 1e9
     traffic = load_traffic()
@@ -347,7 +365,8 @@ def main() -> None:
                 "games_per_gpu": L,
                 "global_games": world * L,
                 "parallelism": f"dp{world} (independent games per GPU)",
-                "step": "nrts_sample_actions + nrts_step",
+                "step": "nrts_sample_actions + nrts_step" if not fused else
+                        "nrts_step with the fused uniform draw of the next actions",
                 "l2": "inputs larger than L2 (per-GPU working set "
                       f"{(bytes_per['total'] + 2 * C * 7 * 4) * L / 1e6:.0f} MB)",
             },
@@ -370,7 +389,7 @@ def main() -> None:
                 "h2d_bytes_per_step": world * L * C * 7 * 4 * 2,
                 "d2h_bytes_per_step": world * (L * C * 7 * 4 * 2 + L * 2 * 4 + L),
             },
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (1 if fused else 2) * args.steps,
             "episodes": {"steps": args.stat_steps, "finished": int(stats[0]), "wins_p0": int(stats[1]),
                          "wins_p1": int(stats[2])},
         }

@@ -72,15 +72,32 @@ typedef struct NrtsExtents {
     int32_t partial_observability;/* 0/1 */
 } NrtsExtents;
 
-/* Per-scenario constants, device pointers. */
+/* Per-scenario constants in the form the kernels read them, filled once by
+ * nrts_prepare_scenario from host arrays and passed by value with every launch. */
+#define NRTS_MAX_HEIGHT 64
+#define NRTS_MAX_TYPES 8
+#define NRTS_TABLE_COLUMNS 15 /* followed by one `produces` column per type */
+typedef struct NrtsScenario {
+    uint64_t terrain_rows[NRTS_MAX_HEIGHT];   /* bit x of row y: wall */
+    uint64_t attack_window[NRTS_MAX_TYPES];   /* attack-window cells within each type's range (0: cannot attack) */
+    uint32_t producible[NRTS_MAX_TYPES];      /* bit t: the type produces type t */
+    uint32_t resource_types;                  /* bit t: type t is a resource */
+    uint32_t stockpile_types;                 /* bit t: type t is a stockpile */
+    int32_t table[NRTS_MAX_TYPES * (NRTS_TABLE_COLUMNS + NRTS_MAX_TYPES)]; /* [T, 15+T], see nrts_prepare_scenario */
+} NrtsScenario;
+
+/* Per-scenario content of a launch. */
 typedef struct NrtsContent {
-    const uint8_t* terrain;       /* [H*W] 0/1 walls */
-    const int32_t* table;         /* [T, 15+T] unit table: cost, hit_points, produce_time, move_time,
-                                     attack_time, harvest_time, attack_range, attack_damage,
-                                     harvest_amount, sight_radius, is_resource, is_stockpile,
-                                     can_harvest, can_move, can_attack, produces[T] */
-    const void* reset[NRTS_LEAVES]; /* one game's reset State, decide(initial_state) */
+    NrtsScenario scenario;          /* host struct, passed by value to the kernels */
+    const void* reset[NRTS_LEAVES]; /* device pointers: one game's reset State, decide(initial_state) */
 } NrtsContent;
+
+/* Fills `out` from host arrays: terrain uint8 [H*W] (0/1 walls) and the unit
+ * table int32 [T, 15+T] with columns cost, hit_points, produce_time,
+ * move_time, attack_time, harvest_time, attack_range, attack_damage,
+ * harvest_amount, sight_radius, is_resource, is_stockpile, can_harvest,
+ * can_move, can_attack, then produces[T] (model/unit_types.py:47-148). */
+int nrts_prepare_scenario(const NrtsExtents* extents, const uint8_t* terrain, const int32_t* table, NrtsScenario* out);
 
 /* A batch of games, device pointers, updated in place. */
 typedef struct NrtsState {
@@ -102,6 +119,12 @@ typedef struct NrtsOutputs {
     int32_t* spawn_overflow;      /* [L, 2] telemetry of the ending state */
     uint8_t* final_feature_maps[2]; /* observation of the ending state, before the reset */
     int32_t* final_scalars[2];
+    /* Optional fused draw of the next actions from the legality rows this
+     * call writes: int32 [L, C, 7] per player, the same values
+     * nrts_sample_actions gives for (sample_seed, sample_counter). */
+    int32_t* sampled_actions[2];
+    uint64_t sample_seed;
+    uint64_t sample_counter;
 } NrtsOutputs;
 
 /* One environment step for every game: decode the action rows, the core step

@@ -51,6 +51,11 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                  : "memory");
 }
 
+// L2 prefetch of a 16-byte-aligned span whose size is a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
@@ -69,6 +74,29 @@ __device__ __forceinline__ int32_t floor_div(int32_t a, int32_t b) {
 }
 
 __device__ __forceinline__ int32_t floor_mod(int32_t a, int32_t b) { return a - floor_div(a, b) * b; }
+
+// lowbias32 (C. Wellons' published 32-bit integer hash): an avalanching mixer.
+__host__ __device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+// Bit position of the k-th (0-based) set bit of v; k < popc(v).
+__device__ __forceinline__ int select32(uint32_t v, int k) {
+    int pos = 0, c = __popc(v & 0xffffu);
+    if (k >= c) { k -= c; v >>= 16; pos += 16; }
+    c = __popc(v & 0xffu);
+    if (k >= c) { k -= c; v >>= 8; pos += 8; }
+    c = __popc(v & 0xfu);
+    if (k >= c) { k -= c; v >>= 4; pos += 4; }
+    c = __popc(v & 0x3u);
+    if (k >= c) { k -= c; v >>= 2; pos += 2; }
+    return pos + (k >= static_cast<int>(v & 1u) ? 1 : 0);
+}
 
 // Four bits -> four 0/1 bytes (bit i to byte i).
 __device__ __forceinline__ uint32_t spread4(uint32_t v) { return (v * 0x00204081u) & 0x01010101u; }

@@ -1,0 +1,415 @@
+// Per-step outputs of a game from its slab: legality rows, both players'
+// feature maps and scalars, and the optional fused draw of the next actions.
+//
+// The epilogue first packs every cell's occupant into one word (the
+// reference's own uint8 encoding, observations/symbolic.py:142-168), builds
+// per-player row bitmaps of occupied cells and of visible cells, computes each
+// owned slot's legality row as three 32-bit words, then streams rows and maps
+// to HBM with 16-byte stores.
+#pragma once
+
+#include <cstdint>
+
+#include "device.cuh"
+#include "game.cuh"
+#include "rules.cuh"
+
+namespace nrts {
+
+// Cell word: the occupant's hp 8 | carried 8 | type+1 8 | max(pending kind, 0) 4 |
+// owner+1 2, and the wall bit 30.  Zero exactly when the cell is free.
+constexpr uint32_t kWallBit = 1u << 30;
+constexpr uint32_t kTypeField = 0x00ff0000u;
+
+__device__ __forceinline__ uint32_t occupant_word(const Game& g, int32_t s) {
+    const uint32_t hp = static_cast<uint32_t>(static_cast<int32_t>(g.hit_points[s])) & 0xffu;
+    const uint32_t carried = static_cast<uint32_t>(g.carried[s]) & 0xffu;
+    const uint32_t type = static_cast<uint32_t>(g.unit_type[s] + 1) & 0xffu;
+    const uint32_t pending = static_cast<uint32_t>(max(static_cast<int32_t>(g.pending_kind[s]), kKindNone)) & 0xfu;
+    const uint32_t owner = static_cast<uint32_t>(g.owner[s] + 1) & 0x3u;
+    return hp | (carried << 8) | (type << 16) | (pending << 24) | (owner << 28);
+}
+
+// Disks of sight of each player's units (observations/visibility.py:70-77).
+template <int kW>
+__device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, uint64_t* vis, int lane) {
+    for (int32_t r = lane; r < 2 * G.h; r += 32) vis[r] = 0ull;
+    __syncwarp();
+    for (int32_t p = lane; p < P.owned; p += 32) {
+        const int32_t s = P.neutral + p;
+        if (!g.active(s)) continue;
+        const int32_t player = p >= P.capacity;
+        const int32_t cell = g.cell[s];
+        const int32_t radius = H.at(clampi(g.unit_type[s], 0, P.types - 1), kSightRadius);
+        const int32_t ux = G.x(cell), uy = G.y(cell);
+        int32_t half = radius;
+        for (int32_t dy = 0; dy <= radius; ++dy) {
+            while (half > 0 && half * half + dy * dy > radius * radius) --half;
+            if (half * half + dy * dy > radius * radius) break;
+            const int32_t lo = max(ux - half, 0), hi = min(ux + half, G.width() - 1);
+            if (lo > hi) continue;
+            const uint64_t bits = (hi - lo == 63) ? ~0ull : (((1ull << (hi - lo + 1)) - 1ull) << lo);
+            if (uy - dy >= 0) atomicOr(reinterpret_cast<unsigned long long*>(&vis[player * G.h + uy - dy]), bits);
+            if (dy > 0 && uy + dy < G.h) atomicOr(reinterpret_cast<unsigned long long*>(&vis[player * G.h + uy + dy]), bits);
+        }
+    }
+    __syncwarp();
+}
+
+// Neighbour facts from occupant words (board.py:23-61 over board_view).
+template <int kW>
+__device__ __forceinline__ void neighbour_word(const Header& H, const Geo<kW>& G, const uint32_t* words, int32_t x, int32_t y, int d,
+                                               bool& free, uint32_t& word) {
+    const int32_t nx = x + dir_dx(d), ny = y + dir_dy(d);
+    const bool on_board = nx >= 0 && nx < G.width() && ny >= 0 && ny < G.h;
+    word = on_board ? words[ny * G.width() + nx] : kWallBit;
+    free = word == 0u;
+}
+
+// Legality row of owned slot p as bits (legality.py:32-64, actions.py:28-41):
+// kind 6 | move 4 | harvest 4 | return 4 | produce direction 4 | produce type T | attack O.
+template <int kW>
+__device__ __forceinline__ void legality_row(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, const uint32_t* words,
+                                             const uint64_t* occ, uint32_t afford0, uint32_t afford1, int32_t p, uint32_t& w0, uint32_t& w1,
+                                             uint32_t& w2) {
+    const int32_t slot = P.neutral + p;
+    w0 = 1u;
+    w1 = w2 = 0u;
+    if (g.birth[slot] == kAbsent || g.pending_kind[slot] != kAbsent) return;  // only KIND_NONE
+    const int32_t actor = clampi(g.unit_type[slot], 0, P.types - 1);
+    const int32_t owner = g.owner[slot];
+    const int32_t carried = g.carried[slot];
+    const int32_t cell = g.cell[slot];
+    const int32_t cx = G.x(cell), cy = G.y(cell);
+    const bool can_move = H.at(actor, kCanMove), can_harvest = H.at(actor, kCanHarvest);
+    uint32_t free = 0, resource = 0, stockpile = 0;
+#pragma unroll
+    for (int d = 0; d < kDirections; ++d) {
+        bool f;
+        uint32_t w;
+        neighbour_word(H, G, words, cx, cy, d, f, w);
+        const bool occupied = (w & kTypeField) != 0u;
+        const int32_t t = clampi(static_cast<int32_t>((w >> 16) & 0xffu) - 1, 0, P.types - 1);
+        const int32_t nowner = static_cast<int32_t>((w >> 28) & 0x3u) - 1;
+        free |= static_cast<uint32_t>(f) << d;
+        resource |= static_cast<uint32_t>(occupied && ((H.resource_types >> t) & 1u)) << d;
+        stockpile |= static_cast<uint32_t>(occupied && ((H.stockpile_types >> t) & 1u) && nowner == owner) << d;
+    }
+    const uint32_t move = can_move ? free : 0u;
+    const uint32_t harvest = (can_harvest && carried == 0) ? resource : 0u;
+    const uint32_t ret = (can_harvest && carried > 0) ? stockpile : 0u;
+    const uint32_t type_ok = H.producible[actor] & (owner > 0 ? afford1 : afford0);
+    const uint32_t pdir = type_ok ? free : 0u;
+    const uint32_t ptype = free ? type_ok : 0u;
+    uint64_t attack = 0;
+    const uint64_t in_range = H.attack_window[actor];
+    if (in_range != 0 && owner >= 0 && owner < kPlayers) {
+        const uint64_t* enemy = occ + (1 - owner) * G.h;
+        const int32_t R = P.radius, side = P.side;
+        const uint64_t row_mask = (1ull << side) - 1ull;
+        const int32_t x0 = cx - R;
+        for (int32_t dy = -R; dy <= R; ++dy) {
+            const int32_t y = cy + dy;
+            if (y < 0 || y >= G.h) continue;
+            const uint64_t bits = enemy[y];
+            const uint64_t window = x0 >= 0 ? (bits >> x0) : (bits << (-x0));
+            attack |= (window & row_mask) << ((dy + R) * side);
+        }
+        attack &= in_range;
+    }
+    const uint32_t kinds = 1u | (static_cast<uint32_t>(move != 0) << kKindMove) | (static_cast<uint32_t>(harvest != 0) << kKindHarvest) |
+                           (static_cast<uint32_t>(ret != 0) << kKindReturn) |
+                           (static_cast<uint32_t>(type_ok != 0 && free != 0) << kKindProduce) |
+                           (static_cast<uint32_t>(attack != 0) << kKindAttack);
+    const int a = kKinds + 4 * kDirections + P.types;  // first attack column
+    const uint64_t lo = static_cast<uint64_t>(kinds) | (static_cast<uint64_t>(move) << 6) | (static_cast<uint64_t>(harvest) << 10) |
+                        (static_cast<uint64_t>(ret) << 14) | (static_cast<uint64_t>(pdir) << 18) |
+                        (static_cast<uint64_t>(ptype) << 22) | (attack << a);
+    const uint64_t hi = attack >> (64 - a);
+    w0 = static_cast<uint32_t>(lo);
+    w1 = static_cast<uint32_t>(lo >> 32);
+    w2 = static_cast<uint32_t>(hi);
+}
+
+// 32 row bits starting at column c of row r (rows of 3 words).
+__device__ __forceinline__ uint32_t row_bits(const uint32_t* rows, int32_t r, int32_t c) {
+    const uint32_t* w = rows + r * 3;
+    const int wi = c >> 5, b = c & 31;
+    const uint32_t a0 = w[wi];
+    const uint32_t a1 = wi < 2 ? w[wi + 1] : 0u;
+    return __funnelshift_r(a0, a1, b);
+}
+
+__device__ __forceinline__ uint32_t chunk_bits(const uint32_t* rows, int32_t r, int32_t c, int32_t width) {
+    const int32_t n0 = min(16, width - c);
+    uint32_t bits = row_bits(rows, r, c) & ((1u << n0) - 1u);
+    if (n0 < 16) bits |= row_bits(rows, r + 1, 0) << n0;
+    return bits;
+}
+
+// One player's legality rows [C, width] of this game, as 0/1 bytes: full
+// 16-byte chunks by vector stores (row and column advanced incrementally),
+// the bytes before the first and after the last full chunk one by one.
+__device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game, uint8_t* out, int lane) {
+    const int32_t width = P.mask_width;
+    const int32_t span = P.capacity * width;
+    uint8_t* base = out + game * static_cast<int64_t>(span);
+    const int32_t head = min(span, static_cast<int32_t>((16u - (reinterpret_cast<uintptr_t>(base) & 15u)) & 15u));
+    const int32_t full = (span - head) >> 4;
+    const int32_t tail_start = head + 16 * full;
+    const int32_t loose = head + (span - tail_start);
+    for (int32_t k = lane; k < loose; k += 32) {
+        const int32_t o = k < head ? k : tail_start + (k - head);
+        const int32_t r = o / width, c = o - r * width;
+        base[o] = static_cast<uint8_t>(row_bits(rows, r, c) & 1u);
+    }
+    if (full == 0) return;
+    const int32_t step = 16 * 32;
+    const int32_t step_rows = step / width, step_cols = step - step_rows * width;
+    const int32_t o = head + 16 * lane;
+    int32_t r = o / width, c = o - r * width;
+    for (int32_t k = lane; k < full; k += 32) {
+        const uint32_t bits = chunk_bits(rows, r, c, width);
+        uint4 v;
+        v.x = spread4(bits & 0xfu);
+        v.y = spread4((bits >> 4) & 0xfu);
+        v.z = spread4((bits >> 8) & 0xfu);
+        v.w = spread4((bits >> 12) & 0xfu);
+        *reinterpret_cast<uint4*>(base + head + 16 * k) = v;
+        r += step_rows;
+        c += step_cols;
+        if (c >= width) {
+            c -= width;
+            ++r;
+        }
+    }
+}
+
+// Feature bytes [hp, carried, owner (1 self, 2 opponent), type+1, pending, terrain]
+// of a cell word seen by `player`, as the low four bytes and the high two.
+__device__ __forceinline__ void features(uint32_t w, int player, bool shown, uint32_t& lo, uint32_t& hi) {
+    if (!shown) w &= kWallBit;
+    const uint32_t owner = (w >> 28) & 0x3u;
+    const uint32_t rel = (player == 0 || owner == 0u) ? owner : 3u - owner;
+    lo = (w & 0xffffu) | (rel << 16) | ((w & kTypeField) << 8);
+    hi = ((w >> 24) & 0xfu) | (((w >> 30) & 1u) << 8);
+}
+
+template <int kW>
+__device__ void write_observation(const Params& P, const Geo<kW>& G, const Game& g, const uint32_t* words, const uint64_t* vis, int player,
+                                  int64_t game, uint8_t* maps, int32_t* scalars, int lane) {
+    if (maps != nullptr) {
+        uint8_t* base = maps + game * static_cast<int64_t>(G.cells) * kFeatures;
+        auto cell_features = [&](int32_t c, uint32_t& lo, uint32_t& hi) {
+            const uint32_t w = words[c];
+            bool shown = true;
+            if (P.partial) {
+                const bool seen = (vis[player * G.h + G.y(c)] >> G.x(c)) & 1ull;
+                shown = ((w >> 28) & 0x3u) == static_cast<uint32_t>(player + 1) || seen;
+            }
+            features(w, player, shown, lo, hi);
+        };
+        if ((G.cells & 7) == 0 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+            // 8 cells = 48 bytes = three 16-byte stores; two cells fill three words.
+            for (int32_t c0 = lane * 8; c0 < G.cells; c0 += 32 * 8) {
+                uint32_t w[12];
+#pragma unroll
+                for (int pair = 0; pair < 4; ++pair) {
+                    uint32_t lo0, hi0, lo1, hi1;
+                    cell_features(c0 + 2 * pair, lo0, hi0);
+                    cell_features(c0 + 2 * pair + 1, lo1, hi1);
+                    w[3 * pair] = lo0;
+                    w[3 * pair + 1] = hi0 | (lo1 << 16);
+                    w[3 * pair + 2] = (lo1 >> 16) | (hi1 << 16);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(base + c0 * kFeatures);
+                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+            }
+        } else {
+            for (int32_t c = lane; c < G.cells; c += 32) {
+                uint32_t lo, hi;
+                cell_features(c, lo, hi);
+                for (int b = 0; b < 4; ++b) base[c * kFeatures + b] = static_cast<uint8_t>(lo >> (8 * b));
+                base[c * kFeatures + 4] = static_cast<uint8_t>(hi);
+                base[c * kFeatures + 5] = static_cast<uint8_t>(hi >> 8);
+            }
+        }
+    }
+    if (scalars != nullptr && lane == 0) {  // symbolic.py:171-180
+        *reinterpret_cast<int4*>(scalars + game * kScalars) =
+            make_int4(g.s[kSRes0 + player], g.s[kSRes0 + 1 - player], g.s[kSTime], g.s[kSAlt]);
+    }
+}
+
+// Per-launch draw key from the caller's (seed, counter); host and device agree.
+__host__ __device__ __forceinline__ uint32_t sample_key(uint64_t seed, uint64_t counter) {
+    uint32_t k = mix32(static_cast<uint32_t>(seed) ^ 0x9e3779b9u);
+    k = mix32(k ^ static_cast<uint32_t>(seed >> 32));
+    k = mix32(k ^ static_cast<uint32_t>(counter));
+    return mix32(k ^ static_cast<uint32_t>(counter >> 32));
+}
+
+// Uniform draw over the set bits of each factor group of one legality row (0
+// when a group has none) for row index t = player * L * C + game * C + slot;
+// identical in the step kernel and in sample_kernel.
+__device__ __forceinline__ void draw_row(uint32_t w0, uint32_t w1, uint32_t w2, int32_t types, uint32_t key, uint32_t t, int32_t* out) {
+    const int a = kKinds + 4 * kDirections + types;
+    const uint64_t lo = static_cast<uint64_t>(w0) | (static_cast<uint64_t>(w1) << 32);
+    const uint64_t attack = (lo >> a) | (static_cast<uint64_t>(w2) << (64 - a));
+    const uint64_t groups[kActionColumns] = {lo & 0x3full, (lo >> 6) & 0xfull, (lo >> 10) & 0xfull, (lo >> 14) & 0xfull,
+                                             (lo >> 18) & 0xfull, (lo >> 22) & ((1ull << types) - 1ull), attack};
+    const uint32_t stream = mix32(key + t * 0x9e3779b9u);
+#pragma unroll
+    for (int f = 0; f < kActionColumns; ++f) {
+        const uint64_t bits = groups[f];
+        const uint32_t low = static_cast<uint32_t>(bits), high = static_cast<uint32_t>(bits >> 32);
+        const int low_count = __popc(low), count = low_count + __popc(high);
+        int value = 0;
+        if (count > 0) {
+            const uint32_t h = mix32(stream ^ (static_cast<uint32_t>(f + 1) * 0x85ebca6bu));
+            const int pick = static_cast<int>(__umulhi(h, static_cast<uint32_t>(count)));
+            value = pick < low_count ? select32(low, pick) : 32 + select32(high, pick - low_count);
+        }
+        out[f] = value;
+    }
+}
+
+// Cell words of every cell and, for the legality rows, row bitmaps of the cells
+// each player occupies (the owner plane of board_view, model/board_view.py:44-69).
+template <int kW>
+__device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, const Game& g, uint32_t* words, uint64_t* occ, bool rows,
+                                           int lane) {
+    auto word_of = [&](int32_t c) {
+        const int32_t s = g.entity_at[c];
+        const uint32_t wall_bit = ((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u;
+        return (s == kAbsent ? 0u : occupant_word(g, s)) | wall_bit;
+    };
+    if constexpr (kW > 0 && kW <= 32) {
+        constexpr int kRowsPerChunk = 32 / kW;
+        constexpr uint32_t kMask = kW == 32 ? ~0u : ((1u << kW) - 1u);
+        for (int32_t base = 0; base < G.cells; base += 32) {
+            const int32_t c = base + lane;
+            const uint32_t w = c < G.cells ? word_of(c) : 0u;
+            if (c < G.cells) words[c] = w;
+            const unsigned m0 = __ballot_sync(kFull, ((w >> 28) & 3u) == 1u);
+            const unsigned m1 = __ballot_sync(kFull, ((w >> 28) & 3u) == 2u);
+            if (rows && lane < kRowsPerChunk) {
+                const int32_t row = base / kW + lane;
+                if (row < G.h) {
+                    occ[row] = (m0 >> (lane * kW)) & kMask;
+                    occ[G.h + row] = (m1 >> (lane * kW)) & kMask;
+                }
+            }
+        }
+    } else if constexpr (kW == 64) {
+        for (int32_t row = 0; row < G.h; ++row) {
+            const int32_t c = row * 64 + lane;
+            const uint32_t lo = word_of(c), hi = word_of(c + 32);
+            words[c] = lo;
+            words[c + 32] = hi;
+            const unsigned lo0 = __ballot_sync(kFull, ((lo >> 28) & 3u) == 1u), hi0 = __ballot_sync(kFull, ((hi >> 28) & 3u) == 1u);
+            const unsigned lo1 = __ballot_sync(kFull, ((lo >> 28) & 3u) == 2u), hi1 = __ballot_sync(kFull, ((hi >> 28) & 3u) == 2u);
+            if (rows && lane == 0) {
+                occ[row] = static_cast<uint64_t>(lo0) | (static_cast<uint64_t>(hi0) << 32);
+                occ[G.h + row] = static_cast<uint64_t>(lo1) | (static_cast<uint64_t>(hi1) << 32);
+            }
+        }
+    } else {
+        if (rows)
+            for (int32_t r = lane; r < 2 * G.h; r += 32) occ[r] = 0ull;
+        __syncwarp();
+        for (int32_t c = lane; c < G.cells; c += 32) {
+            const uint32_t w = word_of(c);
+            words[c] = w;
+            const uint32_t owner = (w >> 28) & 3u;
+            if (rows && owner != 0u) atomicOr(reinterpret_cast<unsigned long long*>(&occ[(owner - 1) * G.h + G.y(c)]), 1ull << G.x(c));
+        }
+    }
+    __syncwarp();
+}
+
+// Zero int32 [count] at dst (4-byte aligned) with 16-byte stores where aligned.
+__device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, int lane) {
+    const int32_t head = min(count, static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2));
+    const int32_t quads = (count - head) >> 2;
+    const int32_t tail = head + 4 * quads;
+    if (lane < head) dst[lane] = 0;
+    uint4* body = reinterpret_cast<uint4*>(dst + head);
+    for (int32_t k = lane; k < quads; k += 32) body[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (lane < count - tail) dst[tail + lane] = 0;
+}
+
+template <int kW>
+__device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
+                              uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2], bool sample, int lane) {
+    const Layout& L = P.layout;
+    uint32_t* words = reinterpret_cast<uint32_t*>(slab + L.word_off);
+    uint64_t* occ = reinterpret_cast<uint64_t*>(slab + L.rows_off);
+    uint64_t* vis = occ + 2 * G.h;
+    uint32_t* rows = reinterpret_cast<uint32_t*>(slab + L.mask_off);
+    const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample;
+    const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
+    cell_words(H, G, g, words, occ, want_masks, lane);
+    if (want_masks) {
+        // Types each player can afford (the balance rule of produce.py:25-35).
+        uint32_t afford0 = 0u, afford1 = 0u;
+        for (int32_t t = 0; t < P.types; ++t) {
+            const int32_t cost = H.at(t, kCost);
+            afford0 |= static_cast<uint32_t>(g.s[kSRes0] >= cost) << t;
+            afford1 |= static_cast<uint32_t>(g.s[kSRes1] >= cost) << t;
+        }
+        if (sample) {  // every row draws 0 unless it holds an available unit (written below)
+            for (int player = 0; player < kPlayers; ++player)
+                zero_words(P.sampled[player] + game * P.capacity * kActionColumns, P.capacity * kActionColumns, lane);
+        }
+        // Rows of slots without an available unit hold only KIND_NONE; the
+        // available ones are listed and computed densely.
+        int16_t* avail = reinterpret_cast<int16_t*>(slab + L.list_off);
+        int32_t A = 0;
+        for (int32_t base = 0; base < P.owned; base += 32) {
+            const int32_t p = base + lane;
+            const bool in = p < P.owned;
+            const bool available = in && g.birth[P.neutral + p] != kAbsent && g.pending_kind[P.neutral + p] == kAbsent;
+            if (in && !available) {
+                rows[3 * p] = 1u;
+                rows[3 * p + 1] = 0u;
+                rows[3 * p + 2] = 0u;
+            }
+            const unsigned m = __ballot_sync(kFull, available);
+            if (available) avail[A + __popc(m & lanes_below(lane))] = static_cast<int16_t>(p);
+            A += __popc(m);
+        }
+        __syncwarp();
+        for (int32_t i = lane; i < A; i += 32) {
+            const int32_t p = avail[i];
+            uint32_t w0, w1, w2;
+            legality_row(P, H, G, g, words, occ, afford0, afford1, p, w0, w1, w2);
+            rows[3 * p] = w0;
+            rows[3 * p + 1] = w1;
+            rows[3 * p + 2] = w2;
+            if (sample) {
+                const int32_t player = p >= P.capacity, local = p - player * P.capacity;
+                const int64_t row = game * P.capacity + local;
+                int32_t a[kActionColumns];
+                draw_row(w0, w1, w2, P.types, P.sample_key, static_cast<uint32_t>(player * P.lanes * P.capacity + row), a);
+                int32_t* dst = P.sampled[player] + row * kActionColumns;
+#pragma unroll
+                for (int f = 0; f < kActionColumns; ++f) dst[f] = a[f];
+            }
+        }
+        __syncwarp();
+        for (int player = 0; player < kPlayers; ++player) {
+            if (masks[player] != nullptr) write_masks(P, rows + player * P.capacity * 3, game, masks[player], lane);
+        }
+    }
+    if (want_obs) {
+        if (P.partial) visibility_rows(P, H, G, g, vis, lane);
+        for (int player = 0; player < kPlayers; ++player)
+            write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], lane);
+    }
+    __syncwarp();
+}
+
+}  // namespace nrts

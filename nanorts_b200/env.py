@@ -221,16 +221,17 @@ class NanoRTS:
             offsets=bucket.attack_offset_capacity, strategy=STRATEGY_CODES[bucket.conflict_strategy],
             max_cycles=scenario.max_cycles, partial_observability=int(partial_observability),
         )
-        self._terrain = torch.from_numpy(scenario.terrain.reshape(-1).astype(np.uint8)).to(self.device)
-        self._table = torch.from_numpy(scenario.table).to(self.device)
         self._reset_rows = {
             name: torch.from_numpy(np.ascontiguousarray(reset[name]).astype(self._shapes[name][1])).to(self.device)
             for name in LEAVES
         }
-        self._content = Content(terrain=_ptr(self._terrain), table=_ptr(self._table))
+        self._content = Content()
+        terrain = np.ascontiguousarray(scenario.terrain.reshape(-1).astype(np.uint8))
+        table = np.ascontiguousarray(scenario.table, dtype=np.int32)
+        check(library().nrts_prepare_scenario(ctypes.byref(self._extents), terrain.ctypes.data, table.ctypes.data,
+                                              ctypes.byref(self._content.scenario)))
         for k, name in enumerate(LEAVES):
             self._content.reset[k] = _ptr(self._reset_rows[name])
-        library()  # fail loudly now when the kernels are missing
 
     # -- buffers ----------------------------------------------------------------
     def _empty_state(self, lanes: int) -> EnvironmentState:
@@ -265,6 +266,16 @@ class NanoRTS:
             buf["final_scalars"] = torch.empty_like(buf["scalars"])
         state._buffers = buf
         return buf
+
+    def _action_buffer(self, state: EnvironmentState, avoid: int | None = None) -> torch.Tensor:
+        buf = self._buffers(state)
+        for name in ("actions", "actions_alt"):
+            if name not in buf:
+                buf[name] = torch.empty((PLAYER_COUNT, state.lanes, self.game.bucket.per_player_capacity, 7),
+                                        dtype=torch.int32, device=self.device)
+        first, second = buf["actions"], buf["actions_alt"]
+        in_first = avoid is not None and first.data_ptr() <= avoid < first.data_ptr() + first.numel() * 4
+        return second if in_first else first
 
     def _state_ptrs(self, state: EnvironmentState) -> StatePtrs:
         ptrs = StatePtrs(environment_root=_ptr(state.environment_root), episode_index=_ptr(state.episode_index))
@@ -307,9 +318,14 @@ class NanoRTS:
         state._masks_current = True
         return self._observations(buf), state
 
-    def step(self, key: Any, state: EnvironmentState, actions: dict[str, torch.Tensor],
-             reset_state: Any = None) -> tuple[dict[str, SymbolicObservation], EnvironmentState, dict, dict, dict]:
-        """env.step (facade.py:107-119): the key is ignored, as in the reference."""
+    def step(self, key: Any, state: EnvironmentState, actions: dict[str, torch.Tensor], reset_state: Any = None, *,
+             sample: tuple[int, int] | None = None) -> tuple[dict[str, SymbolicObservation], EnvironmentState, dict, dict, dict]:
+        """env.step (facade.py:107-119): the key is ignored, as in the reference.
+
+        ``sample=(seed, counter)`` also draws the next actions inside the same
+        kernel from the legality rows it writes (``infos["sampled_actions"]``),
+        the values ``sample_actions`` would return for that seed and counter.
+        """
         del key
         if reset_state is not None:
             raise ModelError("NanoRTS.step refuses a reset_state: auto-reset restarts each game at its own root")
@@ -331,6 +347,12 @@ class NanoRTS:
                 out.final_scalars[p] = _ptr(buf["final_scalars"][p])
         for name in ("reward", "done", "terminated", "truncated", "winner", "spawn_overflow"):
             setattr(out, name, _ptr(buf[name]))
+        sampled = None
+        if sample is not None:
+            # Two action buffers alternate so the draw never overwrites the rows this step reads.
+            sampled = self._action_buffer(state, avoid=rows[0].data_ptr())
+            out.sampled_actions[0], out.sampled_actions[1] = _ptr(sampled[0]), _ptr(sampled[1])
+            out.sample_seed, out.sample_counter = sample[0] & (2**64 - 1), sample[1] & (2**64 - 1)
         ptrs = self._state_ptrs(state)
         check(library().nrts_step(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs), L,
                                   _ptr(rows[0]), _ptr(rows[1]), ctypes.byref(out), self._stream()))
@@ -348,6 +370,8 @@ class NanoRTS:
         }
         if self.final_observation:
             infos["final_observation"] = self._observations(buf, "final_")
+        if sampled is not None:
+            infos["sampled_actions"] = {agent: sampled[p] for p, agent in enumerate(self.agents)}
         return self._observations(buf), state, rewards, dones, infos
 
     def get_avail_actions(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
@@ -386,11 +410,7 @@ class NanoRTS:
         """Uniform legal actions per factor from the current masks (the rollout stand-in for
         per-factor categorical sampling over masked logits, README.md:53-63)."""
         masks = self.get_avail_actions(state)
-        buf = self._buffers(state)
-        if "actions" not in buf:
-            buf["actions"] = torch.empty((PLAYER_COUNT, state.lanes, self.game.bucket.per_player_capacity, 7),
-                                         dtype=torch.int32, device=self.device)
-        acts = buf["actions"]
+        acts = self._action_buffer(state)
         check(library().nrts_sample_actions(ctypes.byref(self._extents), state.lanes, _ptr(masks["player_0"]),
                                             _ptr(masks["player_1"]), _ptr(acts[0]), _ptr(acts[1]),
                                             seed & (2**64 - 1), counter & (2**64 - 1), self._stream()))

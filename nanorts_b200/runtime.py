@@ -31,8 +31,19 @@ class Extents(ctypes.Structure):
     ]
 
 
+MAX_HEIGHT, MAX_TYPES, TABLE_COLUMNS = 64, 8, 15
+
+
+class Scenario(ctypes.Structure):
+    _fields_ = [
+        ("terrain_rows", ctypes.c_uint64 * MAX_HEIGHT), ("attack_window", ctypes.c_uint64 * MAX_TYPES),
+        ("producible", ctypes.c_uint32 * MAX_TYPES), ("resource_types", ctypes.c_uint32),
+        ("stockpile_types", ctypes.c_uint32), ("table", ctypes.c_int32 * (MAX_TYPES * (TABLE_COLUMNS + MAX_TYPES))),
+    ]
+
+
 class Content(ctypes.Structure):
-    _fields_ = [("terrain", ctypes.c_void_p), ("table", ctypes.c_void_p), ("reset", ctypes.c_void_p * LEAF_COUNT)]
+    _fields_ = [("scenario", Scenario), ("reset", ctypes.c_void_p * LEAF_COUNT)]
 
 
 class StatePtrs(ctypes.Structure):
@@ -46,12 +57,13 @@ class Outputs(ctypes.Structure):
         ("reward", ctypes.c_void_p), ("done", ctypes.c_void_p), ("terminated", ctypes.c_void_p),
         ("truncated", ctypes.c_void_p), ("winner", ctypes.c_void_p), ("spawn_overflow", ctypes.c_void_p),
         ("final_feature_maps", ctypes.c_void_p * 2), ("final_scalars", ctypes.c_void_p * 2),
+        ("sampled_actions", ctypes.c_void_p * 2), ("sample_seed", ctypes.c_uint64), ("sample_counter", ctypes.c_uint64),
     ]
 
 
 # Every symbol the header declares.
 SYMBOLS = (
-    "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells", "nrts_sample_actions",
+    "nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells", "nrts_sample_actions",
     "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
 )
 
@@ -70,6 +82,7 @@ def library() -> ctypes.CDLL:
     except OSError as error:
         raise KernelUnavailable(f"cannot load {LIBRARY}: {error}") from error
     p, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32
+    lib.nrts_prepare_scenario.argtypes = [p, p, p, p]
     lib.nrts_step.argtypes = [p, p, p, i64, p, p, p, p]
     lib.nrts_reset.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_legal_masks.argtypes = [p, p, p, i64, p, p, p]
@@ -80,7 +93,7 @@ def library() -> ctypes.CDLL:
     lib.nrts_self_check.argtypes = [p, i64]
     lib.nrts_build_id.restype = ctypes.c_char_p
     lib.nrts_last_error.restype = ctypes.c_char_p
-    for name in ("nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells",
+    for name in ("nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells",
                  "nrts_sample_actions", "nrts_device_status", "nrts_self_check"):
         getattr(lib, name).restype = i32
     _LIB = lib

@@ -125,3 +125,34 @@ def test_parity_garden_of_war():
 def test_parity_long_horizon():
     """Games that run long enough for units to fight and die (default horizon)."""
     run_parity("c2_16x16_random", lanes=48, steps=1200, seed=11, final_observation=False)
+
+
+def test_fused_sampler_matches_standalone_and_oracle():
+    """Actions drawn inside nrts_step equal nrts_sample_actions' on the same
+    rows, and stepping on them keeps the kernel equal to the oracle."""
+    from nanorts_b200.env import make
+    from oracle.oracle import Oracle
+
+    cfg = CONFIGS["c2_16x16_random"]
+    game = cfg.game(200)
+    lanes = 128
+    env = make("NanoRTS", scenario=game, final_observation=False)
+    orc = Oracle(game, lanes)
+    rng = np.random.default_rng(5)
+    keys = random_keys(rng, lanes)
+    _, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
+    orc.reset(keys)
+    actions = env.sample_actions(state, seed=9, counter=0)
+    for t in range(250):
+        host = np.stack([_np(actions[a]) for a in ("player_0", "player_1")], 1)
+        want = orc.step(host)
+        acts = {a: actions[a].clone() for a in actions}
+        obs, state, rewards, dones, infos = env.step(None, state, acts, sample=(9, t + 1))
+        compare_state(state, orc, f"fused step {t}")
+        assert np.array_equal(_np(dones["__all__"]), want["done"])
+        fused = {a: infos["sampled_actions"][a].clone() for a in ("player_0", "player_1")}
+        env.invalidate(state)  # recompute the rows with nrts_legal_masks, then draw with the standalone kernel
+        standalone = env.sample_actions(state, seed=9, counter=t + 1)
+        for a in fused:
+            assert torch.equal(fused[a], standalone[a]), f"step {t}: fused draw differs for {a}"
+        actions = fused
