@@ -239,12 +239,16 @@ def main() -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
 
+    from nanorts_b200.sharding import EpisodeStats, Shard, shard_keys
+
     game = scenario()
     env = make("NanoRTS", scenario=game, final_observation=False, device=device)
     L = args.lanes
-    rng = np.random.default_rng(1234 + rank)
-    keys = torch.from_numpy(rng.integers(0, 2**32, size=(L, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
-    _, state = env.reset(keys.to(device).view(torch.uint32))
+    # Weak scaling: world * L games, each rank steps its contiguous block of L.
+    shard = Shard(rank, world, world * L)
+    rng = np.random.default_rng(1234)
+    all_keys = torch.from_numpy(rng.integers(0, 2**32, size=(world * L, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
+    _, state = env.reset(shard_keys(all_keys, shard).to(device).view(torch.uint32))
     stream = torch.cuda.current_stream(device)
 
     fused = not args.separate_sampler
@@ -263,8 +267,6 @@ def main() -> None:
     torch.cuda.synchronize(device)
 
     # Timed region: K steps, events around every step kernel for the roofline.
-    done_total = torch.zeros((), dtype=torch.int64, device=device)
-    wins = torch.zeros(2, dtype=torch.int64, device=device)
     step_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -289,14 +291,13 @@ def main() -> None:
     step_kernel_ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
 
     # Episode statistics over a further untimed stretch, reduced once over NCCL.
+    stats = EpisodeStats(device)
     for i in range(args.stat_steps):
         _, _, rewards, dones, infos = one_step(10**9 + i)
-        done_total += dones["__all__"].sum()
-        wins += torch.stack([(infos["winner"] == p).logical_and(dones["__all__"]).sum() for p in range(2)])
-    stats = torch.cat([done_total.view(1), wins])
+        stats.add_step(dones["__all__"], infos["winner"], infos["telemetry"].spawn_overflow)
+    episode_stats = stats.reduce()
     timing = torch.tensor([elapsed_ms, step_kernel_ms], dtype=torch.float64, device=device)
     if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.SUM)
         dist.all_reduce(timing, op=dist.ReduceOp.MAX)
     elapsed_ms, step_kernel_ms = timing.tolist()
 
@@ -390,10 +391,9 @@ def main() -> None:
                 "d2h_bytes_per_step": world * (L * C * 7 * 4 * 2 + L * 2 * 4 + L),
             },
             "gpu_launches": (1 if fused else 2) * args.steps,
-            "episodes": {"steps": args.stat_steps, "finished": int(stats[0]), "wins_p0": int(stats[1]),
-                         "wins_p1": int(stats[2])},
+            "episodes": episode_stats,
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(game)
         print(json.dumps(line))
     if world > 1:

@@ -1,0 +1,112 @@
+"""The C ABI without a GPU: the library loads, exports every symbol
+include/nanorts_b200.h declares, prepares scenarios on the host and refuses
+bad arguments before touching the device."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from nanorts_b200 import map_name_to_scenario, runtime
+from nanorts_b200.model import STRATEGY_CODES
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "nanorts_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from nanorts_b200 import build
+
+    build.build()
+    return runtime.library()
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"\b(nrts_[a-z_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert "nrts_step" in names and "nrts_prepare_scenario" in names
+    for name in names:
+        assert hasattr(lib, name), name
+    assert sorted(runtime.SYMBOLS) == names
+
+
+def test_ctypes_layouts_match_the_header(lib, tmp_path):
+    """Struct sizes and offsets as a C compiler lays the header out."""
+    import shutil
+    import subprocess
+
+    compiler = shutil.which("gcc") or shutil.which("cc")
+    if compiler is None:
+        pytest.skip("no C compiler")
+    probe = tmp_path / "layout.c"
+    probe.write_text(
+        '#include <stddef.h>\n#include <stdio.h>\n#include "nanorts_b200.h"\n'
+        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(NrtsExtents), sizeof(NrtsScenario), "
+        "sizeof(NrtsContent), sizeof(NrtsState), sizeof(NrtsOutputs), offsetof(NrtsOutputs, sampled_actions), "
+        "offsetof(NrtsScenario, table)); return 0; }\n")
+    exe = tmp_path / "layout"
+    subprocess.run([compiler, "-I", str(HEADER.parent), str(probe), "-o", str(exe)], check=True)
+    sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert sizes == [ctypes.sizeof(runtime.Extents), ctypes.sizeof(runtime.Scenario), ctypes.sizeof(runtime.Content),
+                     ctypes.sizeof(runtime.StatePtrs), ctypes.sizeof(runtime.Outputs),
+                     runtime.Outputs.sampled_actions.offset, runtime.Scenario.table.offset]
+
+
+def extents_of(game) -> runtime.Extents:
+    b = game.bucket
+    return runtime.Extents(height=b.height, width=b.width, neutral=b.neutral_capacity, capacity=b.per_player_capacity,
+                           types=b.unit_type_capacity, offsets=b.attack_offset_capacity,
+                           strategy=STRATEGY_CODES[b.conflict_strategy], max_cycles=game.max_cycles)
+
+
+def test_prepare_scenario_packs_terrain_and_tables(lib):
+    game = map_name_to_scenario("GardenOfWar64x64", capacity_profile=False, utt="VERSION_ORIGINAL")
+    x = extents_of(game)
+    sc = runtime.Scenario()
+    terrain = np.ascontiguousarray(game.terrain.reshape(-1).astype(np.uint8))
+    table = np.ascontiguousarray(game.table)
+    assert lib.nrts_prepare_scenario(ctypes.byref(x), terrain.ctypes.data, table.ctypes.data, ctypes.byref(sc)) == 0
+    for y in range(64):
+        row = int(sc.terrain_rows[y])
+        assert [(row >> xx) & 1 for xx in range(64)] == list(game.terrain[y].astype(int))
+    assert sc.producible[1] == 1 << 3  # Base -> Worker
+    assert sc.producible[3] == (1 << 1) | (1 << 2)  # Worker -> Base, Barracks
+    assert sc.resource_types == 1 and sc.stockpile_types == 1 << 1
+    assert bin(sc.attack_window[6]).count("1") == 29  # Ranged: range 3 disk in the 7x7 window
+    assert bin(sc.attack_window[3]).count("1") == 5  # Worker: range 1
+    assert sc.attack_window[1] == 0  # a Base cannot attack
+
+
+@pytest.mark.parametrize("field,value", [("width", 65), ("types", 9), ("offsets", 48), ("strategy", 3), ("capacity", 0)])
+def test_bad_extents_are_refused(lib, field, value):
+    game = map_name_to_scenario("basesWorkers8x8")
+    x = extents_of(game)
+    setattr(x, field, value)
+    sc = runtime.Scenario()
+    terrain = np.zeros(64, np.uint8)
+    rc = lib.nrts_prepare_scenario(ctypes.byref(x), terrain.ctypes.data, game.table.ctypes.data, ctypes.byref(sc))
+    assert rc == -1
+    assert lib.nrts_last_error().decode()
+
+
+def test_null_state_is_refused_before_any_launch(lib):
+    game = map_name_to_scenario("basesWorkers8x8")
+    x = extents_of(game)
+    content = runtime.Content()
+    assert lib.nrts_step(ctypes.byref(x), ctypes.byref(content), None, 4, None, None, None, None) == -1
+    assert "null" in lib.nrts_last_error().decode()
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(runtime, "LIBRARY", tmp_path / "absent.so")
+    monkeypatch.setattr(runtime, "_LIB", None)
+    with pytest.raises(runtime.KernelUnavailable):
+        runtime.library()
