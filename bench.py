@@ -345,6 +345,8 @@ def main() -> None:
     peak, peak_kind = load_peaks()
     achieved = bytes_per["total"] * L / (step_kernel_ms * 1e-3) / 1e9
     traffic = load_traffic()
+    if traffic is not None:  # ncu DRAM bytes per env-step -> per launch of L games
+        traffic *= L
     line = None
     if rank == 0:
         value = world * L * args.steps / (elapsed_ms * 1e-3)
@@ -378,6 +380,8 @@ def main() -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
+                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/step_kernel_16x16.md)",
+                "algorithmic_bytes_per_launch": bytes_per["total"] * L,
                 "kernel": "nrts::step_kernel",
                 "kernel_ms": step_kernel_ms,
                 "bytes_per_env_step": bytes_per["total"],
