@@ -30,6 +30,12 @@
  *   nrts_legal_masks   NanoRTS.get_avail_actions (facade.py:172-174 -> core/cuda/legality.cu)
  *   nrts_observe       NanoRTS.get_obs (facade.py:166-170 -> observations/cuda/visibility.cu)
  *   nrts_slot_cells    NanoRTS.get_slot_cells (facade.py:176-178)
+ *   nrts_bot_act       XLA FFI target nanorts_abstraction_act (bots/cuda/abstraction_act.cu:1099-1322),
+ *                      as called by family.act (bots/family.py:34-69 through
+ *                      bots/whole_act.py:113-153) for WorkerRush and LightRush
+ *   nrts_duel_step     bot against bot: seat_commands for both players
+ *                      (bots/seat.py:152-157), core.step (core/__init__.py:46-60) and
+ *                      the lifecycle's auto-reset (adapters/lifecycle.py:53-75), one launch
  *   nrts_build_id      nanorts_build_id (kernels/cuda/registry.cu:201-229)
  *   nrts_self_check    nanorts_self_check (kernels/cuda/registry.cu:201-229)
  */
@@ -157,6 +163,48 @@ int nrts_slot_cells(const NrtsExtents* extents, const NrtsState* state, int64_t 
  * Deterministic in (seed, counter, game, player, slot, factor). */
 int nrts_sample_actions(const NrtsExtents* extents, int64_t lanes, const uint8_t* masks0, const uint8_t* masks1,
                         int32_t* actions0, int32_t* actions1, uint64_t seed, uint64_t counter, void* stream);
+
+/* One player's rush-bot carry: the reference's AbstractActions pytree
+ * (bots/abstraction.py:71-82) as lane-major device buffers.  The nine int32
+ * [L, C] fields are, in order, kind, unit_birth, order, target, target_birth,
+ * base, base_birth, cell, unit_type; trained is uint8 [L, C] (0/1) and
+ * next_order int32 [L].  A new episode starts from empty_actions
+ * (abstraction.py:120-135): every int32 field -1, trained 0, next_order 0. */
+#define NRTS_CARRY_FIELDS 9
+typedef struct NrtsBotCarry {
+    int32_t* field[NRTS_CARRY_FIELDS];
+    uint8_t* trained;
+    int32_t* next_order;
+} NrtsBotCarry;
+
+/* Rush-family strategies (bots/family.py:14-15). */
+enum NrtsBotStrategy { NRTS_WORKER_RUSH = 0, NRTS_BARRACKS_RUSH = 1 };
+
+/* One scripted player: WorkerRush is {NRTS_WORKER_RUSH, -1}; LightRush is
+ * {NRTS_BARRACKS_RUSH, 4} (TYPE_LIGHT, bots/light_rush.py:13-18). */
+typedef struct NrtsBot {
+    int32_t strategy;   /* NrtsBotStrategy */
+    int32_t trained;    /* unit type a BARRACKS_RUSH barracks trains; ignored by WORKER_RUSH */
+    NrtsBotCarry carry; /* updated in place */
+} NrtsBot;
+
+/* family.act of one player's rush bot on every game: the script
+ * (bots/rush.py:225-246) updates the carry, the abstraction layer
+ * (bots/abstraction.py:282-314, one A* search per executing unit) turns it
+ * into Commands.  `commands` is int32 [L, 6, 2, C]: the Commands fields kind,
+ * direction, none_duration, target_cell, produced_type, request_order
+ * (model/commands.py:22-35), each [2, C]; the other player's row is unissued
+ * (-1, -1, 0, -1, -1, -1).  The state is read only. */
+int nrts_bot_act(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+                 int32_t player, const NrtsBot* bot, int32_t* commands, void* stream);
+
+/* One bot-against-bot step for every game: bots[p] chooses player p's
+ * Commands from the step's starting state, then the core step, outcome and
+ * auto-reset as nrts_step; a finished game's carries return to
+ * empty_actions (bots/seat.py:127).  Outputs as nrts_step; masks,
+ * observations and the fused draw are optional (null skips them). */
+int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+                   const NrtsBot* bots, const NrtsOutputs* outputs, void* stream);
 
 /* Status word: the device writes a nonzero code here when a kernel's bounded
  * wait gives up.  Reads it (synchronously), clears it and returns it. */

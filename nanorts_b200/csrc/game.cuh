@@ -37,7 +37,7 @@ enum Column : int {
     kHarvestAmount, kSightRadius, kIsResource, kIsStockpile, kCanHarvest, kCanMove, kCanAttack, kColumns
 };
 
-enum Mode : int { kModeStep = 0, kModeReset = 1, kModeOutputs = 2 };
+enum Mode : int { kModeStep = 0, kModeReset = 1, kModeOutputs = 2, kModeDuel = 3, kModeBotAct = 4 };
 
 // Scalar slots of a game's slab.
 enum Scalar : int {
@@ -67,6 +67,10 @@ struct Layout {
     int32_t word_off;    // uint32 [cells] occupant words
     int32_t rows_off;    // uint64 [4H] occupancy (2) and visibility (2) rows
     int32_t mask_off;    // uint32 [2C * 3 + 2] legality row words
+    // Scripted bots (duel and bot-act launches only; 0 otherwise).
+    int32_t carry_off;   // two players' carries (bots.cuh carry_bytes each)
+    int32_t cmd_off;     // command rows of both players (CmdLayout)
+    int32_t bot_off;     // bot scratch (BotLayout), aliasing the admission scratch
     int32_t bar_off;     // mbarrier
     int32_t aligned;     // every leaf base and row is 16-byte aligned: rows copy whole, one TMA copy per lane
     int32_t total_bytes; // sum of row_bytes
@@ -88,9 +92,55 @@ struct Params {
     int32_t* sampled[kPlayers];  // fused uniform draw of the next actions (optional)
     uint32_t sample_key;         // sample_key(seed, counter)
     NrtsOutputs out;
+    NrtsBot bot[kPlayers];  // duel: both; bot-act: bot[bot_player]
+    int32_t bot_player;     // bot-act: the acting player
+    int32_t* commands;      // bot-act: Commands int32 [L, 6, 2, C]
+    int32_t rank_bits;      // admission rank field width (admission.py:104-115)
     Layout layout;
     NrtsScenario scenario;  // copied to shared memory by every CTA
 };
+
+__host__ __device__ constexpr int32_t round16i(int32_t v) { return (v + 15) & ~15; }
+
+// Command rows in the slab, one entry per owned slot [2C]: what a scripted
+// bot issues and admission reads (Commands, model/commands.py:22-35), plus the
+// 64-bit admission sort keys of requests with explicit ranks.
+struct CmdLayout {
+    int32_t key, target, order, none, kind, dir, ptype, bytes;
+};
+
+__host__ __device__ inline CmdLayout cmd_layout(int32_t owned, int32_t base) {
+    CmdLayout c;
+    int32_t off = base;
+    c.key = off;  off += round16i(owned * 8);
+    c.target = off;  off += round16i(owned * 2);
+    c.order = off;  off += round16i(owned * 2);
+    c.none = off;  off += round16i(owned * 2);
+    c.kind = off;  off += round16i(owned);
+    c.dir = off;  off += round16i(owned);
+    c.ptype = off;  off += round16i(owned);
+    c.bytes = off - base;
+    return c;
+}
+
+struct Cmds {
+    uint64_t* key;
+    int16_t *target, *order, *none;
+    int8_t *kind, *dir, *ptype;  // ptype clamped to [-1, T]: every out-of-range type decides alike
+};
+
+__device__ __forceinline__ Cmds cmd_view(const Params& P, char* slab) {
+    const CmdLayout c = cmd_layout(P.owned, P.layout.cmd_off);
+    Cmds m;
+    m.key = reinterpret_cast<uint64_t*>(slab + c.key);
+    m.target = reinterpret_cast<int16_t*>(slab + c.target);
+    m.order = reinterpret_cast<int16_t*>(slab + c.order);
+    m.none = reinterpret_cast<int16_t*>(slab + c.none);
+    m.kind = reinterpret_cast<int8_t*>(slab + c.kind);
+    m.dir = reinterpret_cast<int8_t*>(slab + c.dir);
+    m.ptype = reinterpret_cast<int8_t*>(slab + c.ptype);
+    return m;
+}
 
 // Per-CTA constants: the launch's NrtsScenario, copied to shared memory.
 struct Header {

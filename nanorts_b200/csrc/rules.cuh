@@ -310,7 +310,13 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
 // admitted.  A request whose own cost exceeds the balance conflicts with every
 // holder (reservations.py:122-135) and scans every slot.
 // ---------------------------------------------------------------------------
-template <int kW>
+//
+// kCmd: the requests are the slab's command rows a scripted bot wrote (kind,
+// direction, none_duration, target cell, produced type and an explicit rank
+// per owned slot) instead of action rows; they are ordered by player, rank,
+// birth with 64-bit keys (admission.py:104-115).  Bots issue commands only to
+// available units, the slots this pass scans.
+template <int kW, bool kCmd = false>
 __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     const int32_t N = P.neutral, C = P.capacity, E = P.entities;
@@ -360,27 +366,13 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
             const int32_t p = list[i];
             const int32_t slot = N + p;
             const int32_t player = p >= C, local = p - player * C;
-            const int32_t* row = P.actions[player] + (game * C + local) * kActionColumns;
-            const int32_t raw = row[0], r1 = row[1], r2 = row[2], r3 = row[3], r4 = row[4], r5 = row[5], r6 = row[6];
-            issued = raw != kAbsent;
-            if (issued) {
-                const int32_t raw_dir = raw == kKindMove ? r1 : raw == kKindHarvest ? r2 : raw == kKindReturn ? r3
-                                        : raw == kKindProduce ? r4 : kAbsent;
-                const int32_t raw_type = raw == kKindProduce ? r5 : kAbsent;
-                const int32_t cell = g.cell[slot];
-                int32_t target = kAbsent;
-                if (raw == kKindAttack) {
-                    const int32_t tx = G.x(cell) + (floor_mod(r6, P.side) - P.radius);
-                    const int32_t ty = G.y(cell) + (floor_div(r6, P.side) - P.radius);
-                    if (tx >= 0 && tx < G.width() && ty >= 0 && ty < G.h) target = ty * G.width() + tx;
-                }
-                // Canonical forms decide exactly like the raw values: kinds outside
-                // [-1, 5] are unknown (duration 0, never legal), directions outside
-                // [0, 3] are off the board, produced types are only clipped or range-checked.
+            // Canonical forms decide exactly like the raw values: kinds outside
+            // [-1, 5] are unknown (duration 0, never legal), directions outside
+            // [0, 3] are off the board, produced types are only clipped or range-checked.
+            auto decide_request = [&](int32_t raw, int32_t raw_dir, int32_t raw_type, int32_t target, int32_t cnone, int32_t cell) {
                 const int32_t ckind = (raw >= kAbsent && raw <= kKindAttack) ? raw : kKinds;
                 const int32_t cdir = (raw_dir >= 0 && raw_dir < kDirections) ? raw_dir : kDirections;
                 const int32_t cptype = clampi(raw_type, kAbsent, P.types);
-                const int32_t cnone = ckind == kKindNone ? 1 : 0;
                 const int32_t requested = action_duration(P, H, g.unit_type[slot], ckind, cnone, cptype);
                 const bool legal = can_execute(P, H, G, g, slot, ckind, cdir, target, cptype);
                 int32_t kind = legal ? ckind : kKindNone;
@@ -405,24 +397,69 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                 r.ptype = narrow8(cptype);
                 r.serial = 0;
                 info[i] = r;
-                keys[i] = (static_cast<uint32_t>(player) << 31) | static_cast<uint32_t>(g.birth[slot]);
+            };
+            if constexpr (kCmd) {
+                const Cmds m = cmd_view(P, slab);
+                const int32_t raw = m.kind[p];
+                issued = raw != kAbsent;
+                if (issued) {
+                    decide_request(raw, m.dir[p], m.ptype[p], m.target[p], m.none[p], g.cell[slot]);
+                    const int32_t rank = m.order[p];
+                    const int32_t rk = clampi(rank == kAbsent ? 0 : rank, 0, (1 << P.rank_bits) - 1);
+                    m.key[i] = (static_cast<uint64_t>((player << P.rank_bits) | rk) << 32) | static_cast<uint32_t>(g.birth[slot]);
+                } else {
+                    m.key[i] = ~0ull;
+                }
             } else {
-                keys[i] = 0xffffffffu;  // sorts after every issued request
+                const int32_t* row = P.actions[player] + (game * C + local) * kActionColumns;
+                const int32_t raw = row[0], r1 = row[1], r2 = row[2], r3 = row[3], r4 = row[4], r5 = row[5], r6 = row[6];
+                issued = raw != kAbsent;
+                if (issued) {
+                    const int32_t raw_dir = raw == kKindMove ? r1 : raw == kKindHarvest ? r2 : raw == kKindReturn ? r3
+                                            : raw == kKindProduce ? r4 : kAbsent;
+                    const int32_t raw_type = raw == kKindProduce ? r5 : kAbsent;
+                    const int32_t cell = g.cell[slot];
+                    int32_t target = kAbsent;
+                    if (raw == kKindAttack) {
+                        const int32_t tx = G.x(cell) + (floor_mod(r6, P.side) - P.radius);
+                        const int32_t ty = G.y(cell) + (floor_div(r6, P.side) - P.radius);
+                        if (tx >= 0 && tx < G.width() && ty >= 0 && ty < G.h) target = ty * G.width() + tx;
+                    }
+                    const int32_t ckind = (raw >= kAbsent && raw <= kKindAttack) ? raw : kKinds;
+                    decide_request(raw, raw_dir, raw_type, target, ckind == kKindNone ? 1 : 0, cell);
+                    keys[i] = (static_cast<uint32_t>(player) << 31) | static_cast<uint32_t>(g.birth[slot]);
+                } else {
+                    keys[i] = 0xffffffffu;  // sorts after every issued request
+                }
             }
         }
         R += __popc(__ballot_sync(kFull, issued));
     }
     __syncwarp();
-    // Java order (admission.py:67-101): player, then birth.
-    for (int32_t i = lane; i < A; i += 32) {
-        const uint32_t k = keys[i];
-        if (k == 0xffffffffu) continue;
-        int32_t rank = 0;
-        for (int32_t j = 0; j < A; ++j) {
-            const uint32_t kj = keys[j];
-            rank += kj < k || (kj == k && j < i);
+    // Java order (admission.py:67-101): player, then (rank,) birth.
+    if constexpr (kCmd) {
+        const uint64_t* keys64 = cmd_view(P, slab).key;
+        for (int32_t i = lane; i < A; i += 32) {
+            const uint64_t k = keys64[i];
+            if (k == ~0ull) continue;
+            int32_t rank = 0;
+            for (int32_t j = 0; j < A; ++j) {
+                const uint64_t kj = keys64[j];
+                rank += kj < k || (kj == k && j < i);
+            }
+            order[rank] = static_cast<int16_t>(i);
         }
-        order[rank] = static_cast<int16_t>(i);
+    } else {
+        for (int32_t i = lane; i < A; i += 32) {
+            const uint32_t k = keys[i];
+            if (k == 0xffffffffu) continue;
+            int32_t rank = 0;
+            for (int32_t j = 0; j < A; ++j) {
+                const uint32_t kj = keys[j];
+                rank += kj < k || (kj == k && j < i);
+            }
+            order[rank] = static_cast<int16_t>(i);
+        }
     }
     __syncwarp();
     // Pending orders by prefix count of appends in admission order; the

@@ -15,6 +15,7 @@
 //   auto-reset        adapters/lifecycle.py:53-75, adapters/jaxmarl/env.py:109-170
 //   legality rows     core/legality.py:32-64, kinds/*.py `_legality`, actions.py:28-41
 //   observations      observations/symbolic.py:130-180, observations/visibility.py:70-77
+//   rush bots         bots/rush.py:24-246, bots/abstraction.py:268-1119, bots/pathfinding.py:125-252
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -27,6 +28,7 @@
 #include "game.cuh"
 #include "outputs.cuh"
 #include "rules.cuh"
+#include "bots.cuh"
 
 namespace nrts {
 
@@ -45,6 +47,48 @@ __device__ Header setup_header(const Params& P, char* smem) {
     H.resource_types = P.scenario.resource_types;
     H.stockpile_types = P.scenario.stockpile_types;
     return H;
+}
+
+// After admission: completion, outcome (outcome.py:11-37) and its outputs,
+// the optional observation of the ending state, and the lifecycle's auto-reset
+// (lifecycle.py:53-75).  Returns whether the game ended.
+template <int kW>
+__device__ __forceinline__ bool finish_core_step(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab,
+                                                 int64_t game, int lane) {
+    complete(P, H, G, g, slab, lane);
+    bool terminated, truncated;
+    decide(P, g, slab, lane, terminated, truncated);
+    const bool done = terminated || truncated;
+    if (lane == 0) {
+        const NrtsOutputs& o = P.out;
+        const int32_t winner = g.s[kSWinner];
+        if (o.reward) {  // outcome.py:32-37
+            reinterpret_cast<float2*>(o.reward)[game] =
+                make_float2(done ? (winner == 0 ? 1.f : -1.f) : 0.f, done ? (winner == 1 ? 1.f : -1.f) : 0.f);
+        }
+        if (o.done) o.done[game] = done;
+        if (o.terminated) o.terminated[game] = terminated;
+        if (o.truncated) o.truncated[game] = truncated;
+        if (o.winner) o.winner[game] = winner;
+        if (o.spawn_overflow) reinterpret_cast<int2*>(o.spawn_overflow)[game] = make_int2(g.s[kSOverflow0], g.s[kSOverflow1]);
+    }
+    if (P.out.final_feature_maps[0] || P.out.final_feature_maps[1] || P.out.final_scalars[0] || P.out.final_scalars[1]) {
+        uint8_t* const no_masks[2] = {nullptr, nullptr};
+        write_outputs(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false, lane);
+    }
+    if (done) {  // lifecycle.advance: the next episode starts from the reset State
+        const int32_t episode = g.s[kSEpisode];
+        const int32_t r0 = g.s[kSRoot0], r1 = g.s[kSRoot1];
+        __syncwarp();
+        load_reset(P, slab, game, lane);
+        if (lane == 0) {
+            g.s[kSEpisode] = static_cast<int32_t>(static_cast<uint32_t>(episode) + 1u);
+            g.s[kSRoot0] = r0;
+            g.s[kSRoot1] = r1;
+        }
+        __syncwarp();
+    }
+    return done;
 }
 
 // One game through the launch's mode; false when a bounded wait gave up.
@@ -66,39 +110,7 @@ __device__ __forceinline__ bool run_game(const Params& P, const Header& H, const
 
     if (P.mode == kModeStep) {
         admit(P, H, G, g, slab, game, lane);
-        complete(P, H, G, g, slab, lane);
-        bool terminated, truncated;
-        decide(P, g, slab, lane, terminated, truncated);
-        const bool done = terminated || truncated;
-        if (lane == 0) {
-            const NrtsOutputs& o = P.out;
-            const int32_t winner = g.s[kSWinner];
-            if (o.reward) {  // outcome.py:32-37
-                reinterpret_cast<float2*>(o.reward)[game] =
-                    make_float2(done ? (winner == 0 ? 1.f : -1.f) : 0.f, done ? (winner == 1 ? 1.f : -1.f) : 0.f);
-            }
-            if (o.done) o.done[game] = done;
-            if (o.terminated) o.terminated[game] = terminated;
-            if (o.truncated) o.truncated[game] = truncated;
-            if (o.winner) o.winner[game] = winner;
-            if (o.spawn_overflow) reinterpret_cast<int2*>(o.spawn_overflow)[game] = make_int2(g.s[kSOverflow0], g.s[kSOverflow1]);
-        }
-        if (P.out.final_feature_maps[0] || P.out.final_feature_maps[1] || P.out.final_scalars[0] || P.out.final_scalars[1]) {
-            uint8_t* const no_masks[2] = {nullptr, nullptr};
-            write_outputs(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false, lane);
-        }
-        if (done) {  // lifecycle.advance: the next episode starts from the reset State
-            const int32_t episode = g.s[kSEpisode];
-            const int32_t r0 = g.s[kSRoot0], r1 = g.s[kSRoot1];
-            __syncwarp();
-            load_reset(P, slab, game, lane);
-            if (lane == 0) {
-                g.s[kSEpisode] = static_cast<int32_t>(static_cast<uint32_t>(episode) + 1u);
-                g.s[kSRoot0] = r0;
-                g.s[kSRoot1] = r1;
-            }
-            __syncwarp();
-        }
+        finish_core_step(P, H, G, g, slab, game, lane);
     }
     if (P.mode != kModeOutputs) store_state(P, slab, game, lane);
     write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, lane);
@@ -130,6 +142,84 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Pa
     for (int64_t game = static_cast<int64_t>(blockIdx.x) * warps + warp; game < P.lanes; game += stride) {
         if (!run_game(P, H, G, slab, bar, parity, game, lane)) break;
         if (P.mode != kModeReset) parity ^= 1u;
+    }
+}
+
+// One game of a bot launch.  Bot-act: the bot of P.bot_player chooses that
+// player's Commands, written to HBM with the settled carry; the State is only
+// read.  Duel: both players' bots choose Commands from the starting State,
+// then the core step as run_game, with the carries of a finished game reset
+// to empty_actions (bots/seat.py:127).
+template <int kW>
+__device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
+                                         uint32_t parity, int64_t game, int lane) {
+    Game g = game_view(P, slab, game);
+    if (!stage_state(P, slab, game, bar, parity, lane)) return false;
+    const bool duel = P.mode == kModeDuel;
+    for (int p = 0; p < kPlayers; ++p) {
+        if (duel || p == P.bot_player) load_carry(P, P.bot[p].carry, carry_view(P, slab, p), game, lane);
+    }
+    __syncwarp();
+    bot_prepare(P, H, G, g, slab, lane);
+    const Cmds cmd = cmd_view(P, slab);
+    for (int p = 0; p < kPlayers; ++p) {
+        if (!duel && p != P.bot_player) continue;
+        BotView v = bot_view(P, g, slab, p);
+        bot_script(P, H, G, v, P.bot[p].strategy, P.bot[p].trained, lane);
+        bot_translate(P, H, G, v, cmd, lane);
+    }
+    if (!duel) {
+        const int32_t C = P.capacity, owned = P.owned;
+        int32_t* out = P.commands + game * 6 * owned;
+        for (int32_t o = lane; o < owned; o += 32) {
+            const bool mine = (o >= C) == (P.bot_player == 1);
+            out[o] = mine ? cmd.kind[o] : kAbsent;
+            out[owned + o] = mine ? cmd.dir[o] : kAbsent;
+            out[2 * owned + o] = mine ? cmd.none[o] : 0;
+            out[3 * owned + o] = mine ? cmd.target[o] : kAbsent;
+            out[4 * owned + o] = mine ? cmd.ptype[o] : kAbsent;
+            out[5 * owned + o] = mine ? cmd.order[o] : kAbsent;
+        }
+        store_carry(P, P.bot[P.bot_player].carry, carry_view(P, slab, P.bot_player), game, lane);
+        __syncwarp();
+        return true;
+    }
+    admit<kW, true>(P, H, G, g, slab, game, lane);
+    if (finish_core_step(P, H, G, g, slab, game, lane)) {
+        empty_carry(P, carry_view(P, slab, 0), lane);
+        empty_carry(P, carry_view(P, slab, 1), lane);
+    }
+    store_state(P, slab, game, lane);
+    for (int p = 0; p < kPlayers; ++p) store_carry(P, P.bot[p].carry, carry_view(P, slab, p), game, lane);
+    const NrtsOutputs& o = P.out;
+    if (o.masks[0] || o.masks[1] || o.feature_maps[0] || o.feature_maps[1] || o.scalars[0] || o.scalars[1] || P.sampled[0])
+        write_outputs(P, H, G, g, slab, game, o.masks, o.feature_maps, o.scalars, P.sampled[0] != nullptr, lane);
+    finish_stores(P, lane);
+    __syncwarp();
+    return true;
+}
+
+template <int kW>
+__global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Params P) {
+    extern __shared__ __align__(128) char smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int warps = blockDim.x >> 5;
+    const Layout& L = P.layout;
+    const Header H = setup_header(P, smem);
+    const Geo<kW> G{P.width, P.height, P.cells};
+    char* slab = smem + L.header_bytes + warp * L.slab_bytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(slab + L.bar_off);
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * warps;
+    uint32_t parity = 0;
+    for (int64_t game = static_cast<int64_t>(blockIdx.x) * warps + warp; game < P.lanes; game += stride) {
+        if (!run_bots(P, H, G, slab, bar, parity, game, lane)) break;
+        parity ^= 1u;
     }
 }
 
@@ -222,7 +312,7 @@ int row_bytes_host(const NrtsExtents* x, int leaf) {
     }
 }
 
-Layout make_layout(const NrtsExtents* x, bool aligned_rows) {
+Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     Layout L{};
     const int E = x->neutral + 2 * x->capacity;
     const int owned = 2 * x->capacity;
@@ -248,7 +338,13 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows) {
     off += round16(E * 2);
     L.free_off = off;
     off += round16(2 * free_words * 4);
-    // Scratch shared by admission, completion and the epilogue, in turn.
+    if (bots) {
+        L.carry_off = off;
+        off += 2 * carry_bytes(x->capacity);
+        L.cmd_off = off;
+        off += cmd_layout(owned, 0).bytes;
+    }
+    // Scratch shared by the bots, admission, completion and the epilogue, in turn.
     const int32_t U = off;
     L.key_off = U;
     L.info_off = U + round16(owned * 4);
@@ -262,6 +358,10 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows) {
     L.mask_off = L.rows_off + round16(4 * x->height * 8);
     const int32_t end_epilogue = L.mask_off + round16((owned * 3 + 2) * 4);
     off = std::max(end_admission, std::max(end_completion, end_epilogue));
+    if (bots) {
+        L.bot_off = U;
+        off = std::max(off, U + bot_layout(x->capacity, E, cells, 0).bytes);
+    }
     L.bar_off = off;
     off += 16;
     L.slab_bytes = round16(off);
@@ -280,7 +380,16 @@ struct DeviceInfo {
 
 DeviceInfo g_devices[64];
 
-const void* pick_kernel(int width) {
+const void* pick_kernel(int width, bool bots = false) {
+    if (bots) {
+        switch (width) {
+            case 8: return reinterpret_cast<const void*>(duel_kernel<8>);
+            case 16: return reinterpret_cast<const void*>(duel_kernel<16>);
+            case 32: return reinterpret_cast<const void*>(duel_kernel<32>);
+            case 64: return reinterpret_cast<const void*>(duel_kernel<64>);
+            default: return reinterpret_cast<const void*>(duel_kernel<0>);
+        }
+    }
     switch (width) {
         case 8: return reinterpret_cast<const void*>(step_kernel<8>);
         case 16: return reinterpret_cast<const void*>(step_kernel<16>);
@@ -298,15 +407,17 @@ int prepare_device(int& device, DeviceInfo*& info) {
         cudaDeviceGetAttribute(&info->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
         cudaDeviceGetAttribute(&info->sms, cudaDevAttrMultiProcessorCount, device);
         for (int w : {8, 16, 32, 64, 7}) {
-            if (cudaFuncSetAttribute(pick_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
-                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(step_kernel) failed");
+            for (bool bots : {false, true}) {
+                if (cudaFuncSetAttribute(pick_kernel(w, bots), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                    return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(step/duel kernel) failed");
+            }
         }
         info->ready = true;
     }
     return NRTS_OK;
 }
 
-int fill_params(Params& P, const NrtsExtents* x, const NrtsContent* content, const NrtsState* state, int64_t lanes) {
+int fill_params(Params& P, const NrtsExtents* x, const NrtsContent* content, const NrtsState* state, int64_t lanes, bool bots = false) {
     if (int rc = validate(x)) return rc;
     if (content == nullptr) return fail(NRTS_E_ARGUMENT, "content is null");
     if (state == nullptr) return fail(NRTS_E_ARGUMENT, "state is null");
@@ -345,13 +456,17 @@ int fill_params(Params& P, const NrtsExtents* x, const NrtsContent* content, con
     P.root = state->environment_root;
     P.episode = state->episode_index;
     P.scenario = content->scenario;
-    P.layout = make_layout(x, aligned);
+    P.layout = make_layout(x, aligned, bots);
+    int bits = 0;
+    for (int v = x->capacity - 1; v > 0; v >>= 1) ++bits;
+    P.rank_bits = bits > 1 ? bits : 1;  // admission.py:104-115
     return NRTS_OK;
 }
 
 template <int kW>
 void launch_instance(const Params& P, unsigned blocks, int threads, size_t smem, cudaStream_t stream) {
-    step_kernel<kW><<<blocks, threads, smem, stream>>>(P);
+    if (P.mode == kModeDuel || P.mode == kModeBotAct) duel_kernel<kW><<<blocks, threads, smem, stream>>>(P);
+    else step_kernel<kW><<<blocks, threads, smem, stream>>>(P);
 }
 
 int launch_step(Params& P, void* stream) {
@@ -362,7 +477,7 @@ int launch_step(Params& P, void* stream) {
     const Layout& L = P.layout;
     if (L.header_bytes + L.slab_bytes > info->smem_optin) return fail(NRTS_E_ARGUMENT, "one game does not fit in shared memory");
     // Warps per CTA with the most games resident per SM (registers and shared memory).
-    const void* kernel = pick_kernel(P.width);
+    const void* kernel = pick_kernel(P.width, P.mode == kModeDuel || P.mode == kModeBotAct);
     int best_warps = 1, best_resident = 0;
     for (int warps = 1; warps <= 8; ++warps) {
         const size_t smem = L.header_bytes + static_cast<size_t>(warps) * L.slab_bytes;
@@ -395,7 +510,19 @@ int launch_step(Params& P, void* stream) {
         default: launch_instance<0>(P, static_cast<unsigned>(blocks), warps * 32, smem, s); break;
     }
     const cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("step kernel launch: ") + cudaGetErrorString(err));
+    if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("kernel launch: ") + cudaGetErrorString(err));
+    return NRTS_OK;
+}
+
+int check_bot(const NrtsExtents* x, const NrtsBot* bot) {
+    if (bot == nullptr) return fail(NRTS_E_ARGUMENT, "bot is null");
+    if (bot->strategy != NRTS_WORKER_RUSH && bot->strategy != NRTS_BARRACKS_RUSH) return fail(NRTS_E_ARGUMENT, "unknown bot strategy");
+    if (x->types <= kTypeWorker) return fail(NRTS_E_ARGUMENT, "the rush bots need the base, barracks and worker unit types");
+    if (bot->strategy == NRTS_BARRACKS_RUSH && (bot->trained < 0 || bot->trained >= x->types))
+        return fail(NRTS_E_ARGUMENT, "a barracks rush needs a trained unit type of the table");
+    for (int f = 0; f < NRTS_CARRY_FIELDS; ++f)
+        if (bot->carry.field[f] == nullptr) return fail(NRTS_E_ARGUMENT, "a carry field is null");
+    if (bot->carry.trained == nullptr || bot->carry.next_order == nullptr) return fail(NRTS_E_ARGUMENT, "a carry field is null");
     return NRTS_OK;
 }
 
@@ -439,6 +566,40 @@ int nrts_reset(const NrtsExtents* extents, const NrtsContent* content, const Nrt
         }
         P.sample_key = sample_key(outputs->sample_seed, outputs->sample_counter);
     }
+    return launch_step(P, stream);
+}
+
+int nrts_bot_act(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes, int32_t player,
+                 const NrtsBot* bot, int32_t* commands, void* stream) {
+    Params P;
+    if (int rc = fill_params(P, extents, content, state, lanes, true)) return rc;
+    if (player != 0 && player != 1) return fail(NRTS_E_ARGUMENT, "player must be 0 or 1");
+    if (int rc = check_bot(extents, bot)) return rc;
+    if (commands == nullptr) return fail(NRTS_E_ARGUMENT, "commands is null");
+    P.mode = kModeBotAct;
+    P.bot_player = player;
+    P.bot[player] = *bot;
+    P.commands = commands;
+    return launch_step(P, stream);
+}
+
+int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes, const NrtsBot* bots,
+                   const NrtsOutputs* outputs, void* stream) {
+    Params P;
+    if (int rc = fill_params(P, extents, content, state, lanes, true)) return rc;
+    if (bots == nullptr) return fail(NRTS_E_ARGUMENT, "bots is null");
+    for (int p = 0; p < kPlayers; ++p)
+        if (int rc = check_bot(extents, &bots[p])) return rc;
+    if (outputs == nullptr) return fail(NRTS_E_ARGUMENT, "outputs is null");
+    if ((outputs->sampled_actions[0] == nullptr) != (outputs->sampled_actions[1] == nullptr))
+        return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
+    P.mode = kModeDuel;
+    P.bot[0] = bots[0];
+    P.bot[1] = bots[1];
+    P.out = *outputs;
+    P.sampled[0] = outputs->sampled_actions[0];
+    P.sampled[1] = outputs->sampled_actions[1];
+    P.sample_key = sample_key(outputs->sample_seed, outputs->sample_counter);
     return launch_step(P, stream);
 }
 
@@ -545,6 +706,8 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
         if (cudaSetDevice(devices[i]) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaSetDevice failed");
         cudaFuncAttributes attributes;
         const void* kernels[] = {pick_kernel(8), pick_kernel(16), pick_kernel(32), pick_kernel(64), pick_kernel(7),
+                                 pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
+                                 pick_kernel(7, true),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
                                  reinterpret_cast<const void*>(probe_kernel)};
         for (const void* k : kernels) {

@@ -61,10 +61,22 @@ class Outputs(ctypes.Structure):
     ]
 
 
+CARRY_FIELDS = 9
+
+
+class BotCarry(ctypes.Structure):
+    _fields_ = [("field", ctypes.c_void_p * CARRY_FIELDS), ("trained", ctypes.c_void_p), ("next_order", ctypes.c_void_p)]
+
+
+class BotSpec(ctypes.Structure):
+    """NrtsBot: strategy, trained unit type, carry."""
+    _fields_ = [("strategy", ctypes.c_int32), ("trained", ctypes.c_int32), ("carry", BotCarry)]
+
+
 # Every symbol the header declares.
 SYMBOLS = (
     "nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells", "nrts_sample_actions",
-    "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
+    "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
 )
 
 _LIB: ctypes.CDLL | None = None
@@ -89,12 +101,14 @@ def library() -> ctypes.CDLL:
     lib.nrts_observe.argtypes = [p, p, p, i64, p, p, p, p, p]
     lib.nrts_slot_cells.argtypes = [p, p, i64, p, p]
     lib.nrts_sample_actions.argtypes = [p, i64, p, p, p, p, ctypes.c_uint64, ctypes.c_uint64, p]
+    lib.nrts_bot_act.argtypes = [p, p, p, i64, i32, p, p, p]
+    lib.nrts_duel_step.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_device_status.argtypes = [ctypes.c_int]
     lib.nrts_self_check.argtypes = [p, i64]
     lib.nrts_build_id.restype = ctypes.c_char_p
     lib.nrts_last_error.restype = ctypes.c_char_p
     for name in ("nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells",
-                 "nrts_sample_actions", "nrts_device_status", "nrts_self_check"):
+                 "nrts_sample_actions", "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_self_check"):
         getattr(lib, name).restype = i32
     _LIB = lib
     return lib

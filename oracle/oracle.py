@@ -54,6 +54,44 @@ class OracleStates(ctypes.Structure):
     ]
 
 
+CARRY_FIELDS = ("kind", "unit_birth", "order", "target", "target_birth", "base", "base_birth", "cell", "unit_type")
+
+# family.py:14-17 strategy numbers; unit_types.py:126 TYPE_LIGHT.
+WORKER_RUSH, BARRACKS_RUSH = 0, 1
+TYPE_LIGHT = 4
+
+
+class OracleCarry(ctypes.Structure):
+    _fields_ = [
+        ("field", ctypes.c_void_p * len(CARRY_FIELDS)),
+        ("trained", ctypes.c_void_p),
+        ("next_order", ctypes.c_void_p),
+    ]
+
+
+def empty_carry(lanes: int, capacity: int) -> dict[str, np.ndarray]:
+    """``abstraction.empty_actions`` per lane (abstraction.py:120-135)."""
+    carry = {name: np.full((lanes, capacity), -1, np.int32) for name in CARRY_FIELDS}
+    carry["trained"] = np.zeros((lanes, capacity), np.uint8)
+    carry["next_order"] = np.zeros(lanes, np.int32)
+    return carry
+
+
+def _carry_struct(carry: dict[str, np.ndarray]) -> OracleCarry:
+    k = OracleCarry(trained=_ptr(carry["trained"]), next_order=_ptr(carry["next_order"]))
+    for f, name in enumerate(CARRY_FIELDS):
+        k.field[f] = _ptr(carry[name])
+    return k
+
+
+def astar(free: np.ndarray, start: int, target: int, range_: int) -> tuple[bool, int, int, int]:
+    """``pathfinding.search`` (program branch) on a bool[H, W] free-cell grid: (found, step, distance, pops)."""
+    free = np.ascontiguousarray(free, np.uint8)
+    out = np.zeros(4, np.int32)
+    lib().oracle_astar(_ptr(free), free.shape[0], free.shape[1], start, target, range_, _ptr(out))
+    return bool(out[0]), int(out[1]), int(out[2]), int(out[3])
+
+
 def build() -> None:
     """Compile the oracle (and, where the reference tree exists, its reference builds)."""
     targets = ["all"]
@@ -76,7 +114,12 @@ def _load() -> ctypes.CDLL:
     lib.oracle_fold_in.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, p]
     lib.oracle_conflict_draw.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
     lib.oracle_conflict_draw.restype = ctypes.c_int32
-    for name in ("oracle_env_step", "oracle_core_step", "oracle_legal_masks", "oracle_observe", "oracle_reset"):
+    lib.oracle_bot_act.argtypes = [p, p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, p, p, ctypes.c_int]
+    lib.oracle_duel_step.argtypes = [p, p, ctypes.c_int64, p, p, p, p] + [p] * 6 + [ctypes.c_int]
+    lib.oracle_astar.argtypes = [p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, p]
+    lib.oracle_astar.restype = None
+    for name in ("oracle_env_step", "oracle_core_step", "oracle_legal_masks", "oracle_observe", "oracle_reset",
+                 "oracle_bot_act", "oracle_duel_step"):
         getattr(lib, name).restype = ctypes.c_int
     return lib
 
@@ -218,6 +261,38 @@ class Oracle:
                                     _ptr(terminated), _ptr(truncated), _ptr(reward), self.threads)
         assert rc == 0, rc
         return {"terminated": terminated.astype(bool), "truncated": truncated.astype(bool), "reward": reward}
+
+    def bot_act(self, player: int, strategy: int, trained: int, carry: dict[str, np.ndarray]) -> np.ndarray:
+        """``family.act`` for one player's rush bot; updates ``carry`` in place, returns Commands int32[L, 6, 2, C]."""
+        commands = np.empty((self.lanes, 6, 2, self.capacity), np.int32)
+        k = _carry_struct(carry)
+        states = self._states()
+        rc = lib().oracle_bot_act(ctypes.byref(self.config), ctypes.byref(states), self.lanes, player, strategy,
+                                  trained, ctypes.byref(k), _ptr(commands), self.threads)
+        assert rc == 0, rc
+        return commands
+
+    def duel_step(self, strategies: tuple[int, int], trained: tuple[int, int],
+                  carries: tuple[dict[str, np.ndarray], dict[str, np.ndarray]]) -> dict[str, np.ndarray]:
+        """Bot against bot: both players' rush bots act, core.step, auto-reset (carries too)."""
+        L = self.lanes
+        st = np.ascontiguousarray(strategies, np.int32)
+        tr = np.ascontiguousarray(trained, np.int32)
+        out = {
+            "reward": np.empty((L, 2), np.float32), "done": np.empty(L, np.uint8),
+            "terminated": np.empty(L, np.uint8), "truncated": np.empty(L, np.uint8),
+            "winner": np.empty(L, np.int32), "spawn_overflow": np.empty((L, 2), np.int32),
+        }
+        k0, k1 = _carry_struct(carries[0]), _carry_struct(carries[1])
+        states = self._states()
+        rc = lib().oracle_duel_step(ctypes.byref(self.config), ctypes.byref(states), L, _ptr(st), _ptr(tr),
+                                    ctypes.byref(k0), ctypes.byref(k1), _ptr(out["reward"]), _ptr(out["done"]),
+                                    _ptr(out["terminated"]), _ptr(out["truncated"]), _ptr(out["winner"]),
+                                    _ptr(out["spawn_overflow"]), self.threads)
+        assert rc == 0, rc
+        for name in ("done", "terminated", "truncated"):
+            out[name] = out[name].astype(bool)
+        return out
 
 
 def sample_uniform_legal(masks: np.ndarray, widths: tuple[int, ...], rng: np.random.Generator) -> np.ndarray:

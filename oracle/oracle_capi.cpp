@@ -10,6 +10,7 @@
 #include <cstring>
 #include <vector>
 
+#include "bots.hpp"
 #include "oracle.hpp"
 
 using namespace oracle;
@@ -39,6 +40,15 @@ struct OracleStates {
     void* leaf[kLeaves];
     uint32_t* environment_root;  // [L, 2]
     uint32_t* episode_index;     // [L]
+};
+
+// One player's bot carry, AbstractActions (bots/abstraction.py:71-82),
+// lane-major: nine int32 [L, C] fields in declaration order, trained
+// uint8 [L, C], next_order int32 [L].
+struct OracleCarry {
+    int32_t* field[9];
+    uint8_t* trained;
+    int32_t* next_order;
 };
 
 }  // extern "C"
@@ -238,6 +248,111 @@ int oracle_reset(const OracleConfig* c, OracleStates* s, int64_t lanes) {
         s->episode_index[lane] = 0u;
     }
     return 0;
+}
+
+static bots::Actions load_carry(const OracleCarry* k, int64_t lane, int32_t C) {
+    bots::Actions a(C);
+    std::vector<int32_t>* fields[9] = {&a.kind, &a.unit_birth, &a.order, &a.target, &a.target_birth,
+                                       &a.base, &a.base_birth, &a.cell, &a.unit_type};
+    for (int f = 0; f < 9; ++f) std::memcpy(fields[f]->data(), k->field[f] + lane * C, 4 * C);
+    std::memcpy(a.trained.data(), k->trained + lane * C, C);
+    a.next_order = k->next_order[lane];
+    return a;
+}
+
+static void store_carry(OracleCarry* k, int64_t lane, int32_t C, const bots::Actions& a) {
+    const std::vector<int32_t>* fields[9] = {&a.kind, &a.unit_birth, &a.order, &a.target, &a.target_birth,
+                                             &a.base, &a.base_birth, &a.cell, &a.unit_type};
+    for (int f = 0; f < 9; ++f) std::memcpy(k->field[f] + lane * C, fields[f]->data(), 4 * C);
+    std::memcpy(k->trained + lane * C, a.trained.data(), C);
+    k->next_order[lane] = a.next_order;
+}
+
+// family.act (bots/family.py:34-81, program branch) for one player's rush
+// bot: the carry is updated in place and `commands` [L, 6, 2, C] receives
+// the Commands fields (kind, direction, none_duration, target_cell,
+// produced_type, request_order); the other player's row is unissued.
+int oracle_bot_act(const OracleConfig* c, OracleStates* s, int64_t lanes, int32_t player, int32_t strategy,
+                   int32_t trained_type, OracleCarry* carry, int32_t* commands, int threads) {
+    if (int e = check(c)) return e;
+    if (player < 0 || player > 1 || strategy < 0 || strategy > 1) return 3;
+    set_threads(threads);
+    const Extents x = extents_of(c);
+    const Content content{c->terrain, c->table, c->types};
+    const int32_t C = x.capacity;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t lane = 0; lane < lanes; ++lane) {
+        Game g = game_at(s->leaf, x, lane);
+        bots::Actions a = load_carry(carry, lane, C);
+        int32_t* base = commands + lane * 6 * 2 * C;
+        static const int32_t empty[6] = {kAbsent, kAbsent, 0, kAbsent, kAbsent, kAbsent};
+        for (int f = 0; f < 6; ++f) std::fill(base + (f * 2 + (1 - player)) * C, base + (f * 2 + (1 - player) + 1) * C, empty[f]);
+        int32_t* rows[6];
+        for (int f = 0; f < 6; ++f) rows[f] = base + (f * 2 + player) * C;
+        const bots::Bot bot{x, content, g, player};
+        bot.act(strategy, trained_type, a, rows);
+        store_carry(carry, lane, C, a);
+    }
+    return 0;
+}
+
+// Bot against bot: each player's commands come from its own rush bot acting
+// on the step's starting state (bots/seat.py:152-157 for one seat, applied to
+// both), then core.step, then the lifecycle's auto-reset
+// (adapters/lifecycle.py:53-75); a finished game's carries go back to
+// empty_actions (bots/seat.py:127).
+int oracle_duel_step(const OracleConfig* c, OracleStates* s, int64_t lanes, const int32_t* strategies, const int32_t* trained,
+                     OracleCarry* carry0, OracleCarry* carry1, float* reward, uint8_t* done, uint8_t* terminated,
+                     uint8_t* truncated, int32_t* winner, int32_t* spawn_overflow, int threads) {
+    if (int e = check(c)) return e;
+    for (int p = 0; p < kPlayers; ++p)
+        if (strategies[p] < 0 || strategies[p] > 1) return 3;
+    set_threads(threads);
+    const Extents x = extents_of(c);
+    const Content content{c->terrain, c->table, c->types};
+    const int32_t C = x.capacity;
+    OracleCarry* carries[kPlayers] = {carry0, carry1};
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t lane = 0; lane < lanes; ++lane) {
+        Game g = game_at(s->leaf, x, lane);
+        Commands cmd(x.owned());
+        bots::Actions acts[kPlayers] = {load_carry(carry0, lane, C), load_carry(carry1, lane, C)};
+        for (int p = 0; p < kPlayers; ++p) {
+            int32_t* rows[6] = {cmd.kind.data() + p * C, cmd.direction.data() + p * C, cmd.none_duration.data() + p * C,
+                                cmd.target_cell.data() + p * C, cmd.produced_type.data() + p * C,
+                                cmd.request_order.data() + p * C};
+            const bots::Bot bot{x, content, g, p};
+            bot.act(strategies[p], trained[p], acts[p], rows);
+        }
+        const StepOutcome out = core_step(g, content, x, cmd, episode_root(s, lane));
+        const bool finished = out.terminated || out.truncated;
+        reward[2 * lane] = out.reward[0];
+        reward[2 * lane + 1] = out.reward[1];
+        done[lane] = finished;
+        terminated[lane] = out.terminated;
+        truncated[lane] = out.truncated;
+        winner[lane] = *g.winner;
+        spawn_overflow[2 * lane] = g.spawn_overflow[0];
+        spawn_overflow[2 * lane + 1] = g.spawn_overflow[1];
+        if (finished) {
+            s->episode_index[lane] += 1u;
+            copy_reset(c, s->leaf, x, lane);
+            acts[0] = bots::Actions(C);
+            acts[1] = bots::Actions(C);
+        }
+        for (int p = 0; p < kPlayers; ++p) store_carry(carries[p], lane, C, acts[p]);
+    }
+    return 0;
+}
+
+// pathfinding.search (program branch): out = {found, step, distance, pops}.
+void oracle_astar(const uint8_t* free, int32_t height, int32_t width, int32_t start, int32_t target, int32_t range, int32_t* out) {
+    const bots::Mask open(free, free + height * width);
+    const bots::Path p = bots::Bot::search(open, start, target, range, height, width);
+    out[0] = p.found;
+    out[1] = p.step;
+    out[2] = p.distance;
+    out[3] = p.pops;
 }
 
 void oracle_threefry2x32(uint32_t k0, uint32_t k1, uint32_t* x0, uint32_t* x1) { threefry2x32(k0, k1, *x0, *x1); }

@@ -49,15 +49,17 @@ def test_ctypes_layouts_match_the_header(lib, tmp_path):
     probe = tmp_path / "layout.c"
     probe.write_text(
         '#include <stddef.h>\n#include <stdio.h>\n#include "nanorts_b200.h"\n'
-        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(NrtsExtents), sizeof(NrtsScenario), "
-        "sizeof(NrtsContent), sizeof(NrtsState), sizeof(NrtsOutputs), offsetof(NrtsOutputs, sampled_actions), "
-        "offsetof(NrtsScenario, table)); return 0; }\n")
+        "int main(void) { printf(\"%zu %zu %zu %zu %zu %zu %zu %zu %zu %zu\\n\", sizeof(NrtsExtents), "
+        "sizeof(NrtsScenario), sizeof(NrtsContent), sizeof(NrtsState), sizeof(NrtsOutputs), "
+        "offsetof(NrtsOutputs, sampled_actions), offsetof(NrtsScenario, table), sizeof(NrtsBotCarry), "
+        "sizeof(NrtsBot), offsetof(NrtsBot, carry)); return 0; }\n")
     exe = tmp_path / "layout"
     subprocess.run([compiler, "-I", str(HEADER.parent), str(probe), "-o", str(exe)], check=True)
     sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     assert sizes == [ctypes.sizeof(runtime.Extents), ctypes.sizeof(runtime.Scenario), ctypes.sizeof(runtime.Content),
                      ctypes.sizeof(runtime.StatePtrs), ctypes.sizeof(runtime.Outputs),
-                     runtime.Outputs.sampled_actions.offset, runtime.Scenario.table.offset]
+                     runtime.Outputs.sampled_actions.offset, runtime.Scenario.table.offset,
+                     ctypes.sizeof(runtime.BotCarry), ctypes.sizeof(runtime.BotSpec), runtime.BotSpec.carry.offset]
 
 
 def extents_of(game) -> runtime.Extents:
@@ -103,6 +105,48 @@ def test_null_state_is_refused_before_any_launch(lib):
     content = runtime.Content()
     assert lib.nrts_step(ctypes.byref(x), ctypes.byref(content), None, 4, None, None, None, None) == -1
     assert "null" in lib.nrts_last_error().decode()
+
+
+def _dummy_state_and_content(game):
+    """Host buffers standing in for device pointers: every call below is refused before any launch."""
+    keep = [np.zeros(4096, np.int32) for _ in range(2 * runtime.LEAF_COUNT + 2)]
+    state, content = runtime.StatePtrs(), runtime.Content()
+    for k in range(runtime.LEAF_COUNT):
+        state.leaf[k] = keep[k].ctypes.data
+        content.reset[k] = keep[runtime.LEAF_COUNT + k].ctypes.data
+    state.environment_root, state.episode_index = keep[-2].ctypes.data, keep[-1].ctypes.data
+    return state, content, keep
+
+
+@pytest.mark.parametrize("strategy,trained,message", [(2, -1, "strategy"), (1, 7, "trained"), (1, -1, "trained")])
+def test_bad_bots_are_refused_before_any_launch(lib, strategy, trained, message):
+    game = map_name_to_scenario("basesWorkers8x8")
+    x = extents_of(game)
+    state, content, keep = _dummy_state_and_content(game)
+    bot = runtime.BotSpec(strategy=strategy, trained=trained)
+    for f in range(runtime.CARRY_FIELDS):
+        bot.carry.field[f] = keep[0].ctypes.data
+    bot.carry.trained = bot.carry.next_order = keep[0].ctypes.data
+    bots = (runtime.BotSpec * 2)(bot, bot)
+    out = runtime.Outputs()
+    assert lib.nrts_duel_step(ctypes.byref(x), ctypes.byref(content), ctypes.byref(state), 4, bots, ctypes.byref(out), None) == -1
+    assert message in lib.nrts_last_error().decode()
+    assert lib.nrts_bot_act(ctypes.byref(x), ctypes.byref(content), ctypes.byref(state), 4, 0, ctypes.byref(bot),
+                            keep[0].ctypes.data, None) == -1
+    assert lib.nrts_bot_act(ctypes.byref(x), ctypes.byref(content), ctypes.byref(state), 4, 2, ctypes.byref(bot),
+                            keep[0].ctypes.data, None) == -1
+    assert "player" in lib.nrts_last_error().decode()
+
+
+def test_null_carry_is_refused(lib):
+    game = map_name_to_scenario("basesWorkers8x8")
+    x = extents_of(game)
+    state, content, keep = _dummy_state_and_content(game)
+    bot = runtime.BotSpec(strategy=0, trained=-1)
+    out = runtime.Outputs()
+    bots = (runtime.BotSpec * 2)(bot, bot)
+    assert lib.nrts_duel_step(ctypes.byref(x), ctypes.byref(content), ctypes.byref(state), 4, bots, ctypes.byref(out), None) == -1
+    assert "carry" in lib.nrts_last_error().decode()
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
