@@ -34,18 +34,33 @@ constexpr int32_t kAbsAttack = 1, kAbsHarvest = 2, kAbsTrain = 3, kAbsBuild = 4,
 constexpr int32_t kFillerDuration = 10;  // abstraction.py:63
 constexpr int32_t kWorkerRush = 0, kBarracksRush = 1;
 constexpr int32_t kTypeBase = 1, kTypeBarracks = 2, kTypeWorker = 3;  // unit_types.py:122-128
+// The carry's int16 order field holds every stamp of a cycle (below 9C + 7).
+constexpr int32_t kMaxBotCapacity = 3600;
 
 // AbstractActions fields (abstraction.py:70-81) in carry order.
 enum CarryField : int { kCKind, kCUnitBirth, kCOrder, kCTarget, kCTargetBirth, kCBase, kCBaseBirth, kCCell, kCUnitType, kCarryFields };
 
-// One player's carry in the slab: nine int32 [C], trained uint8 [C], next_order.
-__host__ __device__ inline int32_t carry_bytes(int32_t C) { return round16i(kCarryFields * 4 * C + round16i(C) + 16); }
+// One player's carry in the slab, each field at its narrowest exact width:
+// births int32; order, target/base slots and the site cell int16 (stamps
+// stay below 9C + 7 within a cycle, settled orders below C); kind, unit type
+// and trained int8.  HBM keeps the reference's int32 leaves.
+struct Carry {
+    int32_t *unit_birth, *target_birth, *base_birth;
+    int16_t *order, *target, *base, *cell;
+    int8_t *kind, *unit_type;
+    uint8_t* trained;
+    int32_t* next_order;
+};
+
+__host__ __device__ inline int32_t carry_bytes(int32_t C) {
+    return 3 * round16i(4 * C) + 4 * round16i(2 * C) + 3 * round16i(C) + 16;
+}
 
 // Bot scratch (aliases the admission/completion scratch, which it precedes).
 struct BotLayout {
     int32_t claimed, free;                                // uint32 [CW]
-    int32_t resources, enemies0, enemies1, stock0, stock1;  // int16 [E]
-    int32_t counts;                                       // int32 [8]
+    int32_t lists;                                        // int16 [2E]: the five unit lists back to back
+    int32_t counts;                                       // int32 [16]: list sizes, list offsets, reserved costs
     int32_t own, brank, enemy, queue, temp;               // int16 [C]
     int32_t standing;                                     // uint8 [C]
     int32_t rows;                                         // PlanRow [C]
@@ -56,12 +71,11 @@ struct BotLayout {
 };
 
 struct PlanRow {
-    int16_t start, goal, radius, target, claimed;
-    int8_t kind, dir, ptype, pad0;
-    int16_t pad1;
+    int16_t start, goal, target, claimed;
+    int8_t kind, dir, ptype, radius;  // attack ranges fit int8 (the attack window is at most 7 wide)
     int32_t cost;
 };
-static_assert(sizeof(PlanRow) == 20, "PlanRow layout");
+static_assert(sizeof(PlanRow) == 16, "PlanRow layout");
 
 __host__ __device__ inline BotLayout bot_layout(int32_t C, int32_t E, int32_t cells, int32_t base) {
     BotLayout b;
@@ -69,12 +83,8 @@ __host__ __device__ inline BotLayout bot_layout(int32_t C, int32_t E, int32_t ce
     int32_t off = base;
     b.claimed = off;  off += round16i(CW * 4);
     b.free = off;  off += round16i(CW * 4);
-    b.resources = off;  off += round16i(E * 2);
-    b.enemies0 = off;  off += round16i(E * 2);
-    b.enemies1 = off;  off += round16i(E * 2);
-    b.stock0 = off;  off += round16i(E * 2);
-    b.stock1 = off;  off += round16i(E * 2);
-    b.counts = off;  off += 32;
+    b.lists = off;  off += round16i(2 * E * 2);
+    b.counts = off;  off += 64;
     b.own = off;  off += round16i(C * 2);
     b.brank = off;  off += round16i(C * 2);
     b.enemy = off;  off += round16i(C * 2);
@@ -91,50 +101,175 @@ __host__ __device__ inline BotLayout bot_layout(int32_t C, int32_t E, int32_t ce
     return b;
 }
 
-enum BotCount : int { kNResources, kNEnemies0, kNEnemies1, kNStock0, kNStock1, kNReserved0, kNReserved1 };
-
-struct Carry {
-    int32_t* f[kCarryFields];
-    uint8_t* trained;
-    int32_t* next_order;
-};
+// counts[]: sizes of the five lists, their offsets in the packed array, the
+// players' reserved PRODUCE costs and the walk's kept count.
+enum BotCount : int { kNResources, kNEnemies0, kNEnemies1, kNStock0, kNStock1, kOffsets, kNReserved0 = 10, kNReserved1, kNKept };
 
 __device__ __forceinline__ Carry carry_view(const Params& P, char* slab, int player) {
-    char* base = slab + P.layout.carry_off + player * carry_bytes(P.capacity);
+    const int32_t C = P.capacity;
+    char* at = slab + P.layout.carry_off + player * carry_bytes(C);
     Carry k;
-    for (int f = 0; f < kCarryFields; ++f) k.f[f] = reinterpret_cast<int32_t*>(base + f * 4 * P.capacity);
-    k.trained = reinterpret_cast<uint8_t*>(base + kCarryFields * 4 * P.capacity);
-    k.next_order = reinterpret_cast<int32_t*>(base + kCarryFields * 4 * P.capacity + round16i(P.capacity));
+    k.unit_birth = reinterpret_cast<int32_t*>(at);  at += round16i(4 * C);
+    k.target_birth = reinterpret_cast<int32_t*>(at);  at += round16i(4 * C);
+    k.base_birth = reinterpret_cast<int32_t*>(at);  at += round16i(4 * C);
+    k.order = reinterpret_cast<int16_t*>(at);  at += round16i(2 * C);
+    k.target = reinterpret_cast<int16_t*>(at);  at += round16i(2 * C);
+    k.base = reinterpret_cast<int16_t*>(at);  at += round16i(2 * C);
+    k.cell = reinterpret_cast<int16_t*>(at);  at += round16i(2 * C);
+    k.kind = reinterpret_cast<int8_t*>(at);  at += round16i(C);
+    k.unit_type = reinterpret_cast<int8_t*>(at);  at += round16i(C);
+    k.trained = reinterpret_cast<uint8_t*>(at);  at += round16i(C);
+    k.next_order = reinterpret_cast<int32_t*>(at);
     return k;
 }
 
-// HBM carry rows of one game <-> the slab (plain coalesced copies).
-__device__ void load_carry(const Params& P, const NrtsBotCarry& src, const Carry& k, int64_t game, int lane) {
+// HBM carries of the acting players -> slab.  Every lane issues all its
+// independent loads of a slot chunk before converting and storing them.
+__device__ void load_carries(const Params& P, char* slab, int64_t game, int lane) {
     const int32_t C = P.capacity;
-    for (int f = 0; f < kCarryFields; ++f) {
-        const int32_t* from = src.field[f] + game * C;
-        for (int32_t i = lane; i < C; i += 32) k.f[f][i] = from[i];
+    for (int p = 0; p < kPlayers; ++p) {
+        if (P.mode != kModeDuel && p != P.bot_player) continue;
+        const NrtsBotCarry& src = P.bot[p].carry;
+        const Carry k = carry_view(P, slab, p);
+        for (int32_t i = lane; i < C; i += 32) {
+            const int64_t at = game * C + i;
+            int32_t v[kCarryFields];
+#pragma unroll
+            for (int f = 0; f < kCarryFields; ++f) v[f] = __ldg(src.field[f] + at);
+            const uint8_t t = __ldg(src.trained + at);
+            k.kind[i] = static_cast<int8_t>(v[kCKind]);
+            k.unit_birth[i] = v[kCUnitBirth];
+            k.order[i] = static_cast<int16_t>(v[kCOrder]);
+            k.target[i] = static_cast<int16_t>(v[kCTarget]);
+            k.target_birth[i] = v[kCTargetBirth];
+            k.base[i] = static_cast<int16_t>(v[kCBase]);
+            k.base_birth[i] = v[kCBaseBirth];
+            k.cell[i] = static_cast<int16_t>(v[kCCell]);
+            k.unit_type[i] = static_cast<int8_t>(v[kCUnitType]);
+            k.trained[i] = t;
+        }
+        if (lane == 0) *k.next_order = __ldg(src.next_order + game);
     }
-    for (int32_t i = lane; i < C; i += 32) k.trained[i] = src.trained[game * C + i];
-    if (lane == 0) *k.next_order = src.next_order[game];
 }
 
-__device__ void store_carry(const Params& P, const NrtsBotCarry& dst, const Carry& k, int64_t game, int lane) {
+// Slab carries of the acting players -> HBM (plain stores).
+__device__ void store_carries(const Params& P, char* slab, int64_t game, int lane) {
     const int32_t C = P.capacity;
-    for (int f = 0; f < kCarryFields; ++f) {
-        int32_t* to = dst.field[f] + game * C;
-        for (int32_t i = lane; i < C; i += 32) to[i] = k.f[f][i];
+    for (int p = 0; p < kPlayers; ++p) {
+        if (P.mode != kModeDuel && p != P.bot_player) continue;
+        const NrtsBotCarry& dst = P.bot[p].carry;
+        const Carry k = carry_view(P, slab, p);
+        for (int32_t i = lane; i < C; i += 32) {
+            const int64_t at = game * C + i;
+            dst.field[kCKind][at] = k.kind[i];
+            dst.field[kCUnitBirth][at] = k.unit_birth[i];
+            dst.field[kCOrder][at] = k.order[i];
+            dst.field[kCTarget][at] = k.target[i];
+            dst.field[kCTargetBirth][at] = k.target_birth[i];
+            dst.field[kCBase][at] = k.base[i];
+            dst.field[kCBaseBirth][at] = k.base_birth[i];
+            dst.field[kCCell][at] = k.cell[i];
+            dst.field[kCUnitType][at] = k.unit_type[i];
+            dst.trained[at] = k.trained[i];
+        }
+        if (lane == 0) dst.next_order[game] = *k.next_order;
     }
-    for (int32_t i = lane; i < C; i += 32) dst.trained[game * C + i] = k.trained[i];
-    if (lane == 0) dst.next_order[game] = *k.next_order;
+}
+
+// The State rows a bot launch moves between HBM and the slab (bot-act reads
+// the State and never writes it back).
+struct RowRef {
+    char* global;
+    char* smem;
+    uint32_t bytes;
+};
+
+__device__ __forceinline__ bool bot_row(const Params& P, char* slab, int64_t game, int r, bool leaves, RowRef& out) {
+    if (r >= kSlabLeaves || !leaves) return false;
+    const Layout& L = P.layout;
+    out.global = global_row(P, r, game);
+    out.smem = slab_row(slab, L, r, out.global);
+    out.bytes = static_cast<uint32_t>(L.row_bytes[r]);
+    return true;
+}
+
+constexpr int kBotRows = kSlabLeaves;
+
+// Copies n < 16 bytes; the loads all issue before the first store.
+__device__ __forceinline__ void copy_edge_in(char* dst, const char* src, uint32_t n) {
+    uint8_t b[15];
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? __ldg(reinterpret_cast<const unsigned char*>(src) + i) : 0;
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i)
+        if (i < n) dst[i] = static_cast<char>(b[i]);
+}
+
+__device__ __forceinline__ void copy_edge_out(char* dst, const char* src, uint32_t n) {
+    uint8_t b[15];
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? static_cast<uint8_t>(src[i]) : 0;
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i)
+        if (i < n) dst[i] = static_cast<char>(b[i]);
+}
+
+// State leaves -> slab in one mbarrier phase, carries while it is in flight.
+// Lane r owns row r: it issues the TMA bulk copy of the row's 16-byte-aligned
+// body and copies the unaligned head and tail bytes itself.
+__device__ bool stage_bots(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane) {
+    RowRef a;
+    const bool has_a = bot_row(P, slab, game, lane, true, a);
+    const Span sa = has_a ? split_row(a.global, a.bytes) : Span{0, 0, 0};
+    const uint32_t total = __reduce_add_sync(kFull, sa.body);
+    if (lane == 0) mbar_arrive_expect_tx(bar, total);
+    __syncwarp();
+    if (sa.body) bulk_load(a.smem + sa.head, a.global + sa.head, sa.body, bar);
+    if (has_a) {
+        copy_edge_in(a.smem, a.global, sa.head);
+        copy_edge_in(a.smem + sa.head + sa.body, a.global + sa.head + sa.body, sa.tail);
+    }
+    load_scalars(P, slab, game, lane);
+    load_carries(P, slab, game, lane);
+    const bool ok = wait_phase(bar, parity);
+    __syncwarp();
+    return ok;
+}
+
+// Slab -> HBM for what a bot launch writes: the State rows (duel), lane r
+// owning row r (TMA bulk store of the body, plain stores of head and tail),
+// and the carries; every lane commits a bulk group and waits for it in
+// finish_bot_stores.
+__device__ void store_bots(const Params& P, char* slab, int64_t game, int lane) {
+    const bool leaves = P.mode == kModeDuel;
+    fence_proxy_async_smem();
+    __syncwarp();
+    for (int r = lane; r < kBotRows; r += 32) {
+        RowRef ref;
+        if (!bot_row(P, slab, game, r, leaves, ref)) continue;
+        const Span sp = split_row(ref.global, ref.bytes);
+        if (sp.body) bulk_store(ref.global + sp.head, ref.smem + sp.head, sp.body);
+        copy_edge_out(ref.global, ref.smem, sp.head);
+        copy_edge_out(ref.global + sp.head + sp.body, ref.smem + sp.head + sp.body, sp.tail);
+    }
+    bulk_commit();
+    if (leaves) store_scalars(P, slab, game, lane);
+    store_carries(P, slab, game, lane);
+}
+
+__device__ __forceinline__ void finish_bot_stores() { bulk_wait_read_all(); }
+
+__device__ __forceinline__ void clear_entry(const Carry& k, int32_t i) {
+    k.unit_birth[i] = k.target_birth[i] = k.base_birth[i] = kAbsent;
+    k.order[i] = k.target[i] = k.base[i] = k.cell[i] = kAbsent;
+    k.kind[i] = k.unit_type[i] = kAbsent;
+    k.trained[i] = 0;
 }
 
 // empty_actions (abstraction.py:120-135).
 __device__ void empty_carry(const Params& P, const Carry& k, int lane) {
     const int32_t C = P.capacity;
-    for (int f = 0; f < kCarryFields; ++f)
-        for (int32_t i = lane; i < C; i += 32) k.f[f][i] = kAbsent;
-    for (int32_t i = lane; i < C; i += 32) k.trained[i] = 0;
+    for (int32_t i = lane; i < C; i += 32) clear_entry(k, i);
     if (lane == 0) *k.next_order = 0;
     __syncwarp();
 }
@@ -160,10 +295,33 @@ __device__ void bot_prepare(const Params& P, const Header& H, const Geo<kW>& G, 
     for (int32_t w = lane; w < CW; w += 32) claimed[w] = 0u;
     __syncwarp();
     int32_t reserved[kPlayers] = {0, 0};
-    int16_t* lists[5] = {reinterpret_cast<int16_t*>(slab + B.resources), reinterpret_cast<int16_t*>(slab + B.enemies0),
-                         reinterpret_cast<int16_t*>(slab + B.enemies1), reinterpret_cast<int16_t*>(slab + B.stock0),
-                         reinterpret_cast<int16_t*>(slab + B.stock1)};
+    int16_t* lists = reinterpret_cast<int16_t*>(slab + B.lists);
+    // Two passes over the slots: list sizes, then members at their offsets.
+    // Resources and the two players' units are disjoint, as are the two
+    // players' stockpiles, so the five lists fit in 2E entries.
+    auto members = [&](int32_t s, bool* member) {
+        const int32_t type = clampi(g.unit_type[s], 0, P.types - 1);
+        const int32_t owner = g.owner[s];
+        member[0] = (H.resource_types >> type) & 1u;
+        member[1] = owner != kAbsent && owner != 0;
+        member[2] = owner != kAbsent && owner != 1;
+        const bool stock = (H.stockpile_types >> type) & 1u;
+        member[3] = stock && owner == 0;
+        member[4] = stock && owner == 1;
+    };
     int32_t n[5] = {0, 0, 0, 0, 0};
+    for (int32_t base = 0; base < E; base += 32) {
+        const int32_t s = base + lane;
+        bool member[5] = {false, false, false, false, false};
+        if (s < E && g.birth[s] != kAbsent) members(s, member);
+#pragma unroll
+        for (int l = 0; l < 5; ++l) n[l] += __popc(__ballot_sync(kFull, member[l]));
+    }
+    int32_t at[5];
+    at[0] = 0;
+#pragma unroll
+    for (int l = 1; l < 5; ++l) at[l] = at[l - 1] + n[l - 1];
+    const int32_t room = 2 * E;
     for (int32_t base = 0; base < E; base += 32) {
         const int32_t s = base + lane;
         bool member[5] = {false, false, false, false, false};
@@ -178,20 +336,14 @@ __device__ void bot_prepare(const Params& P, const Header& H, const Geo<kW>& G, 
             if (pk == kKindProduce && s >= N) {
                 reserved[(s - N) >= C] += H.at(clampi(g.pending_produced_type[s], 0, P.types - 1), kCost);
             }
-            const int32_t type = clampi(g.unit_type[s], 0, P.types - 1);
-            const int32_t owner = g.owner[s];
-            member[0] = (H.resource_types >> type) & 1u;
-            member[1] = owner != kAbsent && owner != 0;
-            member[2] = owner != kAbsent && owner != 1;
-            const bool stock = (H.stockpile_types >> type) & 1u;
-            member[3] = stock && owner == 0;
-            member[4] = stock && owner == 1;
+            members(s, member);
         }
 #pragma unroll
         for (int l = 0; l < 5; ++l) {
             const unsigned m = __ballot_sync(kFull, member[l]);
-            if (member[l]) lists[l][n[l] + __popc(m & lanes_below(lane))] = static_cast<int16_t>(s);
-            n[l] += __popc(m);
+            const int32_t to = at[l] + __popc(m & lanes_below(lane));
+            if (member[l] && to < room) lists[to] = static_cast<int16_t>(s);
+            at[l] += __popc(m);
         }
     }
     reserved[0] = __reduce_add_sync(kFull, reserved[0]);
@@ -203,9 +355,17 @@ __device__ void bot_prepare(const Params& P, const Header& H, const Geo<kW>& G, 
         const unsigned m = __ballot_sync(kFull, open);
         if (lane == 0) free_w[base >> 5] = m;
     }
-    if (lane < 5) counts[lane] = n[lane];
-    if (lane == 5) counts[kNReserved0] = reserved[0];
-    if (lane == 6) counts[kNReserved1] = reserved[1];
+    // Sizes clipped to the packed array (they never exceed it for valid States).
+    int32_t start = 0;
+#pragma unroll
+    for (int l = 0; l < 5; ++l) {
+        const int32_t size = start + n[l] <= room ? n[l] : (start < room ? room - start : 0);
+        if (lane == l) counts[l] = size;
+        if (lane == 5 + l) counts[kOffsets + l] = start;
+        start += n[l];
+    }
+    if (lane == 10) counts[kNReserved0] = reserved[0];
+    if (lane == 11) counts[kNReserved1] = reserved[1];
     __syncwarp();
 }
 
@@ -302,9 +462,9 @@ __device__ __forceinline__ BotView bot_view(const Params& P, const Game& g, char
               reinterpret_cast<uint32_t*>(slab + B.free), reinterpret_cast<uint32_t*>(slab + B.seen),
               reinterpret_cast<uint32_t*>(slab + B.used), reinterpret_cast<uint32_t*>(slab + B.kept),
               reinterpret_cast<uint8_t*>(slab + B.first), reinterpret_cast<int16_t*>(slab + B.stack),
-              reinterpret_cast<const int16_t*>(slab + B.resources),
-              reinterpret_cast<const int16_t*>(slab + (player == 0 ? B.enemies0 : B.enemies1)),
-              reinterpret_cast<const int16_t*>(slab + (player == 0 ? B.stock0 : B.stock1)),
+              reinterpret_cast<const int16_t*>(slab + B.lists) + counts[kOffsets + kNResources],
+              reinterpret_cast<const int16_t*>(slab + B.lists) + counts[kOffsets + (player == 0 ? kNEnemies0 : kNEnemies1)],
+              reinterpret_cast<const int16_t*>(slab + B.lists) + counts[kOffsets + (player == 0 ? kNStock0 : kNStock1)],
               counts[kNResources], counts[player == 0 ? kNEnemies0 : kNEnemies1], counts[player == 0 ? kNStock0 : kNStock1],
               player, P.neutral + player * P.capacity};
     return v;
@@ -314,16 +474,16 @@ __device__ __forceinline__ BotView bot_view(const Params& P, const Game& g, char
 // order a fresh entry takes.
 __device__ __forceinline__ void write_entry(const Carry& k, int32_t i, int32_t birth, int32_t kind, int32_t stamp, int32_t target,
                                             int32_t target_birth, int32_t base, int32_t base_birth, int32_t cell, int32_t unit_type) {
-    const bool known = k.f[kCKind][i] != kAbsent && k.f[kCUnitBirth][i] == birth;
-    if (!known) k.f[kCOrder][i] = stamp;
-    k.f[kCKind][i] = kind;
-    k.f[kCUnitBirth][i] = birth;
-    k.f[kCTarget][i] = target;
-    k.f[kCTargetBirth][i] = target_birth;
-    k.f[kCBase][i] = base;
-    k.f[kCBaseBirth][i] = base_birth;
-    k.f[kCCell][i] = cell;
-    k.f[kCUnitType][i] = unit_type;
+    const bool known = k.kind[i] != kAbsent && k.unit_birth[i] == birth;
+    if (!known) k.order[i] = static_cast<int16_t>(stamp);
+    k.kind[i] = static_cast<int8_t>(kind);
+    k.unit_birth[i] = birth;
+    k.target[i] = static_cast<int16_t>(target);
+    k.target_birth[i] = target_birth;
+    k.base[i] = static_cast<int16_t>(base);
+    k.base_birth[i] = base_birth;
+    k.cell[i] = static_cast<int16_t>(cell);
+    k.unit_type[i] = static_cast<int8_t>(unit_type);
     k.trained[i] = 0;
 }
 
@@ -376,8 +536,8 @@ __device__ void bot_script(const Params& P, const Header& H, const Geo<kW>& G, B
     auto build_if = [&](int32_t builder, int32_t unit_type, int32_t reserved) {
         bool builds = false;
         if (builder >= 0) {
-            const bool building = k.f[kCKind][builder] == kAbsBuild && k.f[kCUnitBirth][builder] == g.birth[bs + builder] &&
-                                  k.f[kCUnitType][builder] == unit_type;
+            const bool building = k.kind[builder] == kAbsBuild && k.unit_birth[builder] == g.birth[bs + builder] &&
+                                  k.unit_type[builder] == unit_type;
             builds = !building;
         }
         const int32_t site = builds ? building_site(P, H, G, g, g.cell[bs + builder], reserved, lane) : kAbsent;
@@ -397,9 +557,9 @@ __device__ void bot_script(const Params& P, const Header& H, const Geo<kW>& G, B
                 const int32_t ss = closest(G, g, v.stock, v.n_stock, cell);
                 const int32_t rb = birth_of(g, rs), sb = birth_of(g, ss);
                 const bool carrying = g.carried[bs + i] > 0;
-                const bool harvesting = k.f[kCKind][i] == kAbsHarvest && k.f[kCUnitBirth][i] == g.birth[bs + i];
-                const bool same_base = k.f[kCBase][i] == ss && k.f[kCBaseBirth][i] == sb;
-                const bool same_target = k.f[kCTarget][i] == rs && k.f[kCTargetBirth][i] == rb;
+                const bool harvesting = k.kind[i] == kAbsHarvest && k.unit_birth[i] == g.birth[bs + i];
+                const bool same_base = k.base[i] == ss && k.base_birth[i] == sb;
+                const bool same_target = k.target[i] == rs && k.target_birth[i] == rb;
                 const bool occupied = carrying ? stock_found : (stock_found && res_found);
                 const bool unchanged = harvesting && same_base && (carrying || same_target);
                 set6(f, carrying ? kAbsent : rs, carrying ? kAbsent : rb, ss, sb, kAbsent, kAbsent);
@@ -567,16 +727,16 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
 
     // _standing (abstraction.py:395-423) and executes; this player's rows unissued.
     for (int32_t i = lane; i < C; i += 32) {
-        const int32_t kind = k.f[kCKind][i];
+        const int32_t kind = k.kind[i];
         const int32_t b = g.birth[bs + i];
-        const bool alive = kind != kAbsent && k.f[kCUnitBirth][i] == b;
+        const bool alive = kind != kAbsent && k.unit_birth[i] == b;
         const bool carrying = g.carried[bs + i] > 0;
-        const bool target_gone = !exists(k.f[kCTarget][i], k.f[kCTargetBirth][i]);
+        const bool target_gone = !exists(k.target[i], k.target_birth[i]);
         bool completed = false;
         if (kind == kAbsAttack) completed = target_gone;
-        else if (kind == kAbsHarvest) completed = carrying ? !exists(k.f[kCBase][i], k.f[kCBaseBirth][i]) : target_gone;
+        else if (kind == kAbsHarvest) completed = carrying ? !exists(k.base[i], k.base_birth[i]) : target_gone;
         else if (kind == kAbsTrain) completed = k.trained[i] != 0;
-        else if (kind == kAbsBuild) completed = k.f[kCCell][i] != kAbsent && g.entity_at[clampi(k.f[kCCell][i], 0, cells - 1)] != kAbsent;
+        else if (kind == kAbsBuild) completed = k.cell[i] != kAbsent && g.entity_at[clampi(k.cell[i], 0, cells - 1)] != kAbsent;
         const bool st = alive && !completed;
         const bool ex = st && b != kAbsent && g.pending_kind[bs + i] == kAbsent;
         v.standing[i] = static_cast<uint8_t>(st ? (ex ? 3 : 1) : 0);
@@ -593,10 +753,10 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
     const int32_t q = warp_compact(C, lane, v.temp, [&](int32_t i) { return v.standing[i] == 3; });
     for (int32_t e = lane; e < q; e += 32) {
         const int32_t i = v.temp[e];
-        const int32_t o = k.f[kCOrder][i];
+        const int32_t o = k.order[i];
         int32_t r = 0;
         for (int32_t j = 0; j < q; ++j) {
-            const int32_t oj = k.f[kCOrder][v.temp[j]];
+            const int32_t oj = k.order[v.temp[j]];
             r += oj < o || (oj == o && j < e);
         }
         v.queue[r] = static_cast<int16_t>(i);
@@ -606,29 +766,27 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
     for (int32_t e = lane; e < q; e += 32) {
         const int32_t i = v.queue[e];
         const int32_t slot = bs + i;
-        const int32_t kind = k.f[kCKind][i];
+        const int32_t kind = k.kind[i];
         const int32_t ucell = g.cell[slot];
         const int32_t utype = clampi(g.unit_type[slot], 0, T - 1);
-        const int32_t target_cell = cell_of(k.f[kCTarget][i]);
+        const int32_t target_cell = cell_of(k.target[i]);
         const int32_t range = H.at(utype, kAttackRange);
         const int32_t tdx = G.x(ucell) - floor_mod(target_cell, G.width()), tdy = G.y(ucell) - floor_div(target_cell, G.width());
         const bool in_range = tdx * tdx + tdy * tdy <= range * range;
         const bool carrying = g.carried[slot] > 0;
-        const int32_t harvest_goal = carrying ? cell_of(k.f[kCBase][i]) : target_cell;
-        const int32_t goal = kind == kAbsAttack ? target_cell : kind == kAbsHarvest ? harvest_goal : kind == kAbsBuild ? k.f[kCCell][i] : kAbsent;
+        const int32_t harvest_goal = carrying ? cell_of(k.base[i]) : target_cell;
+        const int32_t goal = kind == kAbsAttack ? target_cell : kind == kAbsHarvest ? harvest_goal : kind == kAbsBuild ? k.cell[i] : kAbsent;
         const int32_t radius = kind == kAbsAttack ? range : (kind == kAbsHarvest || kind == kAbsBuild) ? 1 : 0;
         const bool searches = goal != kAbsent && !(kind == kAbsAttack && in_range);
         PlanRow row;
         row.start = static_cast<int16_t>(ucell);
         row.goal = static_cast<int16_t>(searches ? goal : ucell);
-        row.radius = static_cast<int16_t>(searches ? radius : 0);
+        row.radius = static_cast<int8_t>(searches ? clampi(radius, 0, 127) : 0);
         row.target = kAbsent;
         row.claimed = kAbsent;
         row.kind = kAbsent;
         row.dir = kAbsent;
         row.ptype = kAbsent;
-        row.pad0 = 0;
-        row.pad1 = 0;
         row.cost = 0;
         if (kind == kAbsAttack) {  // strike
             if (in_range && target_cell != kAbsent) {
@@ -643,9 +801,9 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
             }
         } else if (kind == kAbsTrain || kind == kAbsBuild) {  // train / adjacent production (_production, :465-484)
             int32_t dir = kAbsent;
-            const int32_t produced = k.f[kCUnitType][i];
+            const int32_t produced = k.unit_type[i];
             if (kind == kAbsBuild) {
-                dir = adjacent_direction(G, ucell, k.f[kCCell][i]);
+                dir = adjacent_direction(G, ucell, k.cell[i]);
             } else {  // _training_direction (abstraction.py:487-511)
                 const bool harvests = H.at(clampi(produced, 0, T - 1), kCanHarvest) != 0;
                 const int16_t* near = harvests ? v.resources : v.enemies;
@@ -734,10 +892,10 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
                 cmd.order[o] = static_cast<int16_t>(kept_count++);
             }
         }
-        v.counts[7] = kept_count;
+        v.counts[kNKept] = kept_count;
     }
     __syncwarp();
-    const int32_t kept_count = v.counts[7];
+    const int32_t kept_count = v.counts[kNKept];
     // _commands (abstraction.py:1068-1096): available units without a kept desire wait.
     const int32_t nf = warp_compact(C, lane, v.temp, [&](int32_t i) {
         return g.birth[bs + i] != kAbsent && g.pending_kind[bs + i] == kAbsent && cmd.kind[p * C + i] == kAbsent;
@@ -758,9 +916,9 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
     for (int32_t i = lane; i < C; i += 32) {
         int32_t r = kAbsent;
         if (v.standing[i] != 0) {
-            const int32_t o = k.f[kCOrder][i];
+            const int32_t o = k.order[i];
             r = 0;
-            for (int32_t j = 0; j < ns; ++j) r += k.f[kCOrder][v.temp[j]] < o;
+            for (int32_t j = 0; j < ns; ++j) r += k.order[v.temp[j]] < o;
         }
         v.brank[i] = static_cast<int16_t>(r);
     }
@@ -768,13 +926,12 @@ __device__ void bot_translate(const Params& P, const Header& H, const Geo<kW>& G
     for (int32_t i = lane; i < C; i += 32) {
         const uint8_t st = v.standing[i];
         if (st != 0) {
-            const int32_t kind = k.f[kCKind][i];
+            const int32_t kind = k.kind[i];
             const bool trains = kind == kAbsTrain || kind == kAbsTrainDirection;
             k.trained[i] = static_cast<uint8_t>(k.trained[i] != 0 || (st == 3 && trains));
-            k.f[kCOrder][i] = v.brank[i];
+            k.order[i] = v.brank[i];
         } else {
-            for (int f = 0; f < kCarryFields; ++f) k.f[f][i] = kAbsent;
-            k.trained[i] = 0;
+            clear_entry(k, i);
         }
     }
     if (lane == 0) *k.next_order = ns;

@@ -103,16 +103,14 @@ struct Params {
 __host__ __device__ constexpr int32_t round16i(int32_t v) { return (v + 15) & ~15; }
 
 // Command rows in the slab, one entry per owned slot [2C]: what a scripted
-// bot issues and admission reads (Commands, model/commands.py:22-35), plus the
-// 64-bit admission sort keys of requests with explicit ranks.
+// bot issues and admission reads (Commands, model/commands.py:22-35).
 struct CmdLayout {
-    int32_t key, target, order, none, kind, dir, ptype, bytes;
+    int32_t target, order, none, kind, dir, ptype, bytes;
 };
 
 __host__ __device__ inline CmdLayout cmd_layout(int32_t owned, int32_t base) {
     CmdLayout c;
     int32_t off = base;
-    c.key = off;  off += round16i(owned * 8);
     c.target = off;  off += round16i(owned * 2);
     c.order = off;  off += round16i(owned * 2);
     c.none = off;  off += round16i(owned * 2);
@@ -124,7 +122,6 @@ __host__ __device__ inline CmdLayout cmd_layout(int32_t owned, int32_t base) {
 }
 
 struct Cmds {
-    uint64_t* key;
     int16_t *target, *order, *none;
     int8_t *kind, *dir, *ptype;  // ptype clamped to [-1, T]: every out-of-range type decides alike
 };
@@ -132,7 +129,6 @@ struct Cmds {
 __device__ __forceinline__ Cmds cmd_view(const Params& P, char* slab) {
     const CmdLayout c = cmd_layout(P.owned, P.layout.cmd_off);
     Cmds m;
-    m.key = reinterpret_cast<uint64_t*>(slab + c.key);
     m.target = reinterpret_cast<int16_t*>(slab + c.target);
     m.order = reinterpret_cast<int16_t*>(slab + c.order);
     m.none = reinterpret_cast<int16_t*>(slab + c.none);
@@ -288,6 +284,30 @@ __device__ bool wait_phase(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// The game's scalar leaves -> slab scalars, one per lane.
+__device__ __forceinline__ void load_scalars(const Params& P, char* slab, int64_t game, int lane) {
+    const Layout& L = P.layout;
+    int32_t* s = reinterpret_cast<int32_t*>(slab + L.scal_off);
+    const int32_t* res = static_cast<const int32_t*>(P.leaf[NRTS_PLAYER_RESOURCES]);
+    const int32_t* ov = static_cast<const int32_t*>(P.leaf[NRTS_SPAWN_OVERFLOW]);
+    switch (lane) {
+        case kSTime: s[kSTime] = static_cast<const int32_t*>(P.leaf[NRTS_TIME])[game]; break;
+        case kSRes0: s[kSRes0] = res[2 * game]; break;
+        case kSRes1: s[kSRes1] = res[2 * game + 1]; break;
+        case kSNextBirth: s[kSNextBirth] = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_BIRTH])[game]; break;
+        case kSNextOrder: s[kSNextOrder] = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_PENDING_ORDER])[game]; break;
+        case kSAlt: s[kSAlt] = static_cast<const int32_t*>(P.leaf[NRTS_ALTERNATING_CONFLICT_COUNT])[game]; break;
+        case kSGameOver: s[kSGameOver] = static_cast<const uint8_t*>(P.leaf[NRTS_GAME_OVER])[game]; break;
+        case kSWinner: s[kSWinner] = static_cast<const int32_t*>(P.leaf[NRTS_WINNER])[game]; break;
+        case kSOverflow0: s[kSOverflow0] = ov[2 * game]; break;
+        case kSOverflow1: s[kSOverflow1] = ov[2 * game + 1]; break;
+        case kSEpisode: s[kSEpisode] = static_cast<int32_t>(P.episode[game]); break;
+        case kSRoot0: s[kSRoot0] = static_cast<int32_t>(P.root[2 * game]); break;
+        case kSRoot1: s[kSRoot1] = static_cast<int32_t>(P.root[2 * game + 1]); break;
+        default: break;
+    }
+}
+
 // Global rows -> slab; scalar leaves -> slab scalars.
 __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane) {
     const Layout& L = P.layout;
@@ -322,25 +342,7 @@ __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t*
         for (uint32_t i = lane; i < sp.head; i += 32) dst[i] = src[i];
         for (uint32_t i = lane; i < sp.tail; i += 32) dst[sp.head + sp.body + i] = src[sp.head + sp.body + i];
     }
-    int32_t* s = reinterpret_cast<int32_t*>(slab + L.scal_off);
-    const int32_t* res = static_cast<const int32_t*>(P.leaf[NRTS_PLAYER_RESOURCES]);
-    const int32_t* ov = static_cast<const int32_t*>(P.leaf[NRTS_SPAWN_OVERFLOW]);
-    switch (lane) {
-        case kSTime: s[kSTime] = static_cast<const int32_t*>(P.leaf[NRTS_TIME])[game]; break;
-        case kSRes0: s[kSRes0] = res[2 * game]; break;
-        case kSRes1: s[kSRes1] = res[2 * game + 1]; break;
-        case kSNextBirth: s[kSNextBirth] = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_BIRTH])[game]; break;
-        case kSNextOrder: s[kSNextOrder] = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_PENDING_ORDER])[game]; break;
-        case kSAlt: s[kSAlt] = static_cast<const int32_t*>(P.leaf[NRTS_ALTERNATING_CONFLICT_COUNT])[game]; break;
-        case kSGameOver: s[kSGameOver] = static_cast<const uint8_t*>(P.leaf[NRTS_GAME_OVER])[game]; break;
-        case kSWinner: s[kSWinner] = static_cast<const int32_t*>(P.leaf[NRTS_WINNER])[game]; break;
-        case kSOverflow0: s[kSOverflow0] = ov[2 * game]; break;
-        case kSOverflow1: s[kSOverflow1] = ov[2 * game + 1]; break;
-        case kSEpisode: s[kSEpisode] = static_cast<int32_t>(P.episode[game]); break;
-        case kSRoot0: s[kSRoot0] = static_cast<int32_t>(P.root[2 * game]); break;
-        case kSRoot1: s[kSRoot1] = static_cast<int32_t>(P.root[2 * game + 1]); break;
-        default: break;
-    }
+    load_scalars(P, slab, game, lane);
     const bool ok = wait_phase(bar, parity);
     __syncwarp();
     return ok;
@@ -378,6 +380,30 @@ __device__ void load_reset(const Params& P, char* slab, int64_t game, int lane) 
     __syncwarp();
 }
 
+// Slab scalars -> the game's scalar leaves, one per lane.
+__device__ __forceinline__ void store_scalars(const Params& P, char* slab, int64_t game, int lane) {
+    const Layout& L = P.layout;
+    const int32_t* s = reinterpret_cast<const int32_t*>(slab + L.scal_off);
+    int32_t* res = static_cast<int32_t*>(P.leaf[NRTS_PLAYER_RESOURCES]);
+    int32_t* ov = static_cast<int32_t*>(P.leaf[NRTS_SPAWN_OVERFLOW]);
+    switch (lane) {
+        case kSTime: static_cast<int32_t*>(P.leaf[NRTS_TIME])[game] = s[kSTime]; break;
+        case kSRes0: res[2 * game] = s[kSRes0]; break;
+        case kSRes1: res[2 * game + 1] = s[kSRes1]; break;
+        case kSNextBirth: static_cast<int32_t*>(P.leaf[NRTS_NEXT_BIRTH])[game] = s[kSNextBirth]; break;
+        case kSNextOrder: static_cast<int32_t*>(P.leaf[NRTS_NEXT_PENDING_ORDER])[game] = s[kSNextOrder]; break;
+        case kSAlt: static_cast<int32_t*>(P.leaf[NRTS_ALTERNATING_CONFLICT_COUNT])[game] = s[kSAlt]; break;
+        case kSGameOver: static_cast<uint8_t*>(P.leaf[NRTS_GAME_OVER])[game] = static_cast<uint8_t>(s[kSGameOver]); break;
+        case kSWinner: static_cast<int32_t*>(P.leaf[NRTS_WINNER])[game] = s[kSWinner]; break;
+        case kSOverflow0: ov[2 * game] = s[kSOverflow0]; break;
+        case kSOverflow1: ov[2 * game + 1] = s[kSOverflow1]; break;
+        case kSEpisode: P.episode[game] = static_cast<uint32_t>(s[kSEpisode]); break;
+        case kSRoot0: P.root[2 * game] = static_cast<uint32_t>(s[kSRoot0]); break;
+        case kSRoot1: P.root[2 * game + 1] = static_cast<uint32_t>(s[kSRoot1]); break;
+        default: break;
+    }
+}
+
 // Slab -> global rows (TMA bulk stores of the bodies), scalars -> leaves.
 // Every lane that issued stores must later wait for its bulk group (finish_stores).
 __device__ void store_state(const Params& P, char* slab, int64_t game, int lane) {
@@ -405,25 +431,7 @@ __device__ void store_state(const Params& P, char* slab, int64_t game, int lane)
         for (uint32_t i = lane; i < sp.head; i += 32) dst[i] = src[i];
         for (uint32_t i = lane; i < sp.tail; i += 32) dst[sp.head + sp.body + i] = src[sp.head + sp.body + i];
     }
-    const int32_t* s = reinterpret_cast<const int32_t*>(slab + L.scal_off);
-    int32_t* res = static_cast<int32_t*>(P.leaf[NRTS_PLAYER_RESOURCES]);
-    int32_t* ov = static_cast<int32_t*>(P.leaf[NRTS_SPAWN_OVERFLOW]);
-    switch (lane) {
-        case kSTime: static_cast<int32_t*>(P.leaf[NRTS_TIME])[game] = s[kSTime]; break;
-        case kSRes0: res[2 * game] = s[kSRes0]; break;
-        case kSRes1: res[2 * game + 1] = s[kSRes1]; break;
-        case kSNextBirth: static_cast<int32_t*>(P.leaf[NRTS_NEXT_BIRTH])[game] = s[kSNextBirth]; break;
-        case kSNextOrder: static_cast<int32_t*>(P.leaf[NRTS_NEXT_PENDING_ORDER])[game] = s[kSNextOrder]; break;
-        case kSAlt: static_cast<int32_t*>(P.leaf[NRTS_ALTERNATING_CONFLICT_COUNT])[game] = s[kSAlt]; break;
-        case kSGameOver: static_cast<uint8_t*>(P.leaf[NRTS_GAME_OVER])[game] = static_cast<uint8_t>(s[kSGameOver]); break;
-        case kSWinner: static_cast<int32_t*>(P.leaf[NRTS_WINNER])[game] = s[kSWinner]; break;
-        case kSOverflow0: ov[2 * game] = s[kSOverflow0]; break;
-        case kSOverflow1: ov[2 * game + 1] = s[kSOverflow1]; break;
-        case kSEpisode: P.episode[game] = static_cast<uint32_t>(s[kSEpisode]); break;
-        case kSRoot0: P.root[2 * game] = static_cast<uint32_t>(s[kSRoot0]); break;
-        case kSRoot1: P.root[2 * game + 1] = static_cast<uint32_t>(s[kSRoot1]); break;
-        default: break;
-    }
+    store_scalars(P, slab, game, lane);
 }
 
 // Waits until the slab rows read by this lane's bulk stores may be reused.

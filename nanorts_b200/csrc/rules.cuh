@@ -313,9 +313,11 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
 //
 // kCmd: the requests are the slab's command rows a scripted bot wrote (kind,
 // direction, none_duration, target cell, produced type and an explicit rank
-// per owned slot) instead of action rows; they are ordered by player, rank,
-// birth with 64-bit keys (admission.py:104-115).  Bots issue commands only to
-// available units, the slots this pass scans.
+// per owned slot) instead of action rows.  Admission orders requests by
+// player, rank, birth (admission.py:67-115); Commands hold, per player, either
+// no ranks or a permutation of ranks (model/commands.py:37-66), so the key
+// (player, rank) or (player, birth) orders them alike.  Bots issue commands
+// only to available units, the slots this pass scans.
 template <int kW, bool kCmd = false>
 __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
@@ -405,10 +407,11 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                 if (issued) {
                     decide_request(raw, m.dir[p], m.ptype[p], m.target[p], m.none[p], g.cell[slot]);
                     const int32_t rank = m.order[p];
-                    const int32_t rk = clampi(rank == kAbsent ? 0 : rank, 0, (1 << P.rank_bits) - 1);
-                    m.key[i] = (static_cast<uint64_t>((player << P.rank_bits) | rk) << 32) | static_cast<uint32_t>(g.birth[slot]);
+                    const uint32_t minor = rank == kAbsent ? static_cast<uint32_t>(g.birth[slot])
+                                                           : static_cast<uint32_t>(clampi(rank, 0, (1 << P.rank_bits) - 1));
+                    keys[i] = (static_cast<uint32_t>(player) << 31) | minor;
                 } else {
-                    m.key[i] = ~0ull;
+                    keys[i] = 0xffffffffu;
                 }
             } else {
                 const int32_t* row = P.actions[player] + (game * C + local) * kActionColumns;
@@ -436,20 +439,8 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         R += __popc(__ballot_sync(kFull, issued));
     }
     __syncwarp();
-    // Java order (admission.py:67-101): player, then (rank,) birth.
-    if constexpr (kCmd) {
-        const uint64_t* keys64 = cmd_view(P, slab).key;
-        for (int32_t i = lane; i < A; i += 32) {
-            const uint64_t k = keys64[i];
-            if (k == ~0ull) continue;
-            int32_t rank = 0;
-            for (int32_t j = 0; j < A; ++j) {
-                const uint64_t kj = keys64[j];
-                rank += kj < k || (kj == k && j < i);
-            }
-            order[rank] = static_cast<int16_t>(i);
-        }
-    } else {
+    // Java order (admission.py:67-101): player, then rank or birth.
+    {
         for (int32_t i = lane; i < A; i += 32) {
             const uint32_t k = keys[i];
             if (k == 0xffffffffu) continue;

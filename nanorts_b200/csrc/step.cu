@@ -154,12 +154,8 @@ template <int kW>
 __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
                                          uint32_t parity, int64_t game, int lane) {
     Game g = game_view(P, slab, game);
-    if (!stage_state(P, slab, game, bar, parity, lane)) return false;
+    if (!stage_bots(P, slab, game, bar, parity, lane)) return false;
     const bool duel = P.mode == kModeDuel;
-    for (int p = 0; p < kPlayers; ++p) {
-        if (duel || p == P.bot_player) load_carry(P, P.bot[p].carry, carry_view(P, slab, p), game, lane);
-    }
-    __syncwarp();
     bot_prepare(P, H, G, g, slab, lane);
     const Cmds cmd = cmd_view(P, slab);
     for (int p = 0; p < kPlayers; ++p) {
@@ -180,7 +176,8 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
             out[4 * owned + o] = mine ? cmd.ptype[o] : kAbsent;
             out[5 * owned + o] = mine ? cmd.order[o] : kAbsent;
         }
-        store_carry(P, P.bot[P.bot_player].carry, carry_view(P, slab, P.bot_player), game, lane);
+        store_bots(P, slab, game, lane);
+        finish_bot_stores();
         __syncwarp();
         return true;
     }
@@ -189,12 +186,11 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
         empty_carry(P, carry_view(P, slab, 0), lane);
         empty_carry(P, carry_view(P, slab, 1), lane);
     }
-    store_state(P, slab, game, lane);
-    for (int p = 0; p < kPlayers; ++p) store_carry(P, P.bot[p].carry, carry_view(P, slab, p), game, lane);
+    store_bots(P, slab, game, lane);
     const NrtsOutputs& o = P.out;
     if (o.masks[0] || o.masks[1] || o.feature_maps[0] || o.feature_maps[1] || o.scalars[0] || o.scalars[1] || P.sampled[0])
         write_outputs(P, H, G, g, slab, game, o.masks, o.feature_maps, o.scalars, P.sampled[0] != nullptr, lane);
-    finish_stores(P, lane);
+    finish_bot_stores();
     __syncwarp();
     return true;
 }
@@ -514,10 +510,15 @@ int launch_step(Params& P, void* stream) {
     return NRTS_OK;
 }
 
-int check_bot(const NrtsExtents* x, const NrtsBot* bot) {
+int check_bot(const NrtsExtents* x, const NrtsContent* content, const NrtsBot* bot) {
     if (bot == nullptr) return fail(NRTS_E_ARGUMENT, "bot is null");
+    for (int t = 0; t < x->types; ++t) {
+        const int32_t range = content->scenario.table[t * (kColumns + x->types) + kAttackRange];
+        if (range < 0 || range > 127) return fail(NRTS_E_ARGUMENT, "the rush bots take attack ranges between 0 and 127");
+    }
     if (bot->strategy != NRTS_WORKER_RUSH && bot->strategy != NRTS_BARRACKS_RUSH) return fail(NRTS_E_ARGUMENT, "unknown bot strategy");
     if (x->types <= kTypeWorker) return fail(NRTS_E_ARGUMENT, "the rush bots need the base, barracks and worker unit types");
+    if (x->capacity > kMaxBotCapacity) return fail(NRTS_E_ARGUMENT, "the rush bots take at most 3600 slots per player");
     if (bot->strategy == NRTS_BARRACKS_RUSH && (bot->trained < 0 || bot->trained >= x->types))
         return fail(NRTS_E_ARGUMENT, "a barracks rush needs a trained unit type of the table");
     for (int f = 0; f < NRTS_CARRY_FIELDS; ++f)
@@ -574,7 +575,7 @@ int nrts_bot_act(const NrtsExtents* extents, const NrtsContent* content, const N
     Params P;
     if (int rc = fill_params(P, extents, content, state, lanes, true)) return rc;
     if (player != 0 && player != 1) return fail(NRTS_E_ARGUMENT, "player must be 0 or 1");
-    if (int rc = check_bot(extents, bot)) return rc;
+    if (int rc = check_bot(extents, content, bot)) return rc;
     if (commands == nullptr) return fail(NRTS_E_ARGUMENT, "commands is null");
     P.mode = kModeBotAct;
     P.bot_player = player;
@@ -589,7 +590,7 @@ int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const
     if (int rc = fill_params(P, extents, content, state, lanes, true)) return rc;
     if (bots == nullptr) return fail(NRTS_E_ARGUMENT, "bots is null");
     for (int p = 0; p < kPlayers; ++p)
-        if (int rc = check_bot(extents, &bots[p])) return rc;
+        if (int rc = check_bot(extents, content, &bots[p])) return rc;
     if (outputs == nullptr) return fail(NRTS_E_ARGUMENT, "outputs is null");
     if ((outputs->sampled_actions[0] == nullptr) != (outputs->sampled_actions[1] == nullptr))
         return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
