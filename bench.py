@@ -9,6 +9,12 @@ current masks (nrts_sample_actions) + one environment step of every game
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--lanes L] [--impl reference]
 
+``--workload duel`` measures BASELINE.json's configs[3] instead: bot against
+bot on basesWorkers16x16 (VERSION_ORIGINAL, CANCEL_BOTH), player 0 WorkerRush,
+player 1 LightRush, 32768 games per GPU from their reset, auto-reset at the end
+of each game, no masks or observations.  One step = one nrts_duel_step launch
+(both bots' Commands, the core step, the auto-reset of State and carries).
+
 Under torchrun each rank steps its own L games (weak scaling, no collective
 on the step path); one NCCL all-reduce of episode statistics runs after the
 timed region.  Rank 0 prints one JSON line.
@@ -28,14 +34,38 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 METRIC = "env steps/sec (both players, incl. masks+obs)"
+DUEL_METRIC = "env steps/sec (bot vs bot: both bots' commands + core step + auto-reset)"
 MAP, UTT, STRATEGY = "basesWorkers16x16", "VERSION_ORIGINAL", "CANCEL_RANDOM"
-DEFAULT_LANES = 16384
+DUEL_STRATEGY = "CANCEL_BOTH"
+DEFAULT_LANES = {"random": 16384, "duel": 32768}
+# family.py strategy numbers and trained types of WorkerRush (player 0) and LightRush (player 1).
+DUEL_BOTS = ((0, -1), (1, 4))
 
 
-def scenario():
+def scenario(workload: str = "random"):
     from nanorts_b200 import map_name_to_scenario
 
-    return map_name_to_scenario(MAP, utt=UTT, conflict_strategy=STRATEGY, max_cycles=5000)
+    strategy = DUEL_STRATEGY if workload == "duel" else STRATEGY
+    return map_name_to_scenario(MAP, utt=UTT, conflict_strategy=strategy, max_cycles=5000)
+
+
+def duel_algorithmic_bytes(game) -> dict[str, int]:
+    """Bytes one bot-against-bot env-step must move: the State read and written
+    in place, both players' carries (nine int32 fields, trained, next_order per
+    slot block) read and written, and the step outputs."""
+    b = game.bucket
+    E, HW, C = b.entity_capacity, b.cell_count, b.per_player_capacity
+    state = 35 * E + 2 * HW + 37 + 12
+    carry = 37 * C + 4
+    parts = {
+        "state_read": state,
+        "state_write": state,
+        "carries_read": 2 * carry,
+        "carries_write": 2 * carry,
+        "outputs": 8 + 1 + 1 + 1 + 4 + 8,
+    }
+    parts["total"] = sum(parts.values())
+    return parts
 
 
 def algorithmic_bytes(game) -> dict[str, int]:
@@ -64,9 +94,10 @@ def load_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def load_traffic() -> float | None:
-    """DRAM bytes per env-step of the step kernel from the committed ncu summary."""
-    path = ROOT / "profiles" / "step_kernel_16x16_traffic.txt"
+def load_traffic(workload: str = "random") -> float | None:
+    """DRAM bytes per env-step of the measured kernel from the committed ncu summary."""
+    name = "duel_kernel_16x16_traffic.txt" if workload == "duel" else "step_kernel_16x16_traffic.txt"
+    path = ROOT / "profiles" / name
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
@@ -163,12 +194,73 @@ def cpu_baseline(game, seconds: float = 12.0, lanes: int = 512, threads: int | N
     }
 
 
+def duel_cpu_baseline(game, seconds: float = 12.0, lanes: int = 256, threads: int | None = None) -> dict:
+    """The CPU oracle's bot-against-bot step (C++ restatement of the reference's
+    JAX program path for WorkerRush/LightRush and core.step, OpenMP over games)
+    on a bounded sample: `lanes` games from their reset, stepped for `seconds`."""
+    from oracle.oracle import Oracle, empty_carry
+
+    threads = threads or os.cpu_count() or 1
+    orc = Oracle(game, lanes, threads=threads)
+    orc.reset(np.zeros((lanes, 2), np.uint32))
+    C = game.bucket.per_player_capacity
+    carries = (empty_carry(lanes, C), empty_carry(lanes, C))
+    strategies, trained = tuple(b[0] for b in DUEL_BOTS), tuple(b[1] for b in DUEL_BOTS)
+    for _ in range(3):
+        orc.duel_step(strategies, trained, carries)
+    steps, start = 0, time.perf_counter()
+    while time.perf_counter() - start < seconds:
+        orc.duel_step(strategies, trained, carries)
+        steps += 1
+    elapsed = time.perf_counter() - start
+    return {
+        "value": lanes * steps / elapsed,
+        "unit": "env-steps/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{lanes} games x {steps} steps of {MAP}/{DUEL_STRATEGY} WorkerRush vs LightRush from the reset, "
+                  f"C++ oracle bots + core step + auto-reset, {threads} OpenMP threads",
+    }
+
+
 def run_reference(args) -> None:
     """--impl reference: the reference's CPU path for this workload.  The reference
     (JAX) cannot be installed here, so this times the C++ oracle port of its JAX
     program on the host cores; each step is a bounded sample of the workload."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "duel":
+        game = scenario("duel")
+        from oracle.oracle import Oracle, empty_carry
+
+        threads = os.cpu_count() or 1
+        lanes = 256
+        orc = Oracle(game, lanes, threads=threads)
+        orc.reset(np.zeros((lanes, 2), np.uint32))
+        C = game.bucket.per_player_capacity
+        carries = (empty_carry(lanes, C), empty_carry(lanes, C))
+        strategies, trained = tuple(b[0] for b in DUEL_BOTS), tuple(b[1] for b in DUEL_BOTS)
+        for _ in range(args.warmup):
+            orc.duel_step(strategies, trained, carries)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            orc.duel_step(strategies, trained, carries)
+        elapsed = time.perf_counter() - t0
+        value = lanes * args.steps / elapsed
+        print(json.dumps({
+            "impl": "reference",
+            "metric": DUEL_METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int32", "data": "synthetic",
+            "config": {"workload": f"{MAP} {UTT} {DUEL_STRATEGY}, WorkerRush vs LightRush, auto-reset",
+                       "lanes_per_step_sample": lanes, "full_lanes": args.lanes},
+            "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
+                             "sample": f"{lanes} games per step on {threads} threads; the reference's JAX CPU path is "
+                                       "not runnable here (jax absent, reference install failed), so its C++ "
+                                       "restatement runs"},
+            "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
         return
     game = scenario()
     from oracle.oracle import Oracle, sample_uniform_legal
@@ -210,16 +302,23 @@ def main() -> None:
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=20)
-    parser.add_argument("--lanes", type=int, default=DEFAULT_LANES, help="games per GPU")
+    parser.add_argument("--workload", default="random", choices=("random", "duel"),
+                        help="random: configs[1] (uniform legal actions); duel: configs[3] (WorkerRush vs LightRush)")
+    parser.add_argument("--lanes", type=int, default=None, help="games per GPU")
     parser.add_argument("--impl", default="nanorts_b200", choices=("nanorts_b200", "reference"))
     parser.add_argument("--e2e-steps", type=int, default=50)
-    parser.add_argument("--stat-steps", type=int, default=200)
+    parser.add_argument("--stat-steps", type=int, default=None,
+                        help="untimed steps whose episode statistics are reduced (default 200; duel 600, about one game)")
     parser.add_argument("--separate-sampler", action="store_true",
                         help="draw actions with nrts_sample_actions instead of inside nrts_step")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
+    if args.lanes is None:
+        args.lanes = DEFAULT_LANES[args.workload]
+    if args.stat_steps is None:
+        args.stat_steps = 600 if args.workload == "duel" else 200
     if args.impl == "reference":
         run_reference(args)
         return
@@ -241,6 +340,9 @@ def main() -> None:
 
     from nanorts_b200.sharding import EpisodeStats, Shard, shard_keys
 
+    if args.workload == "duel":
+        run_duel(args, world, rank, local, device)
+        return
     game = scenario()
     env = make("NanoRTS", scenario=game, final_observation=False, device=device)
     L = args.lanes
@@ -399,6 +501,147 @@ def main() -> None:
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(game)
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_duel(args, world: int, rank: int, local: int, device) -> None:
+    """WorkerRush (player 0) against LightRush (player 1), one
+    nrts_duel_step launch per step, every game from its reset and restarting
+    when it ends.  The bots read no host input, so the end-to-end number times
+    the same launches plus the per-step read-back of rewards, dones and winners."""
+    import torch
+    import torch.distributed as dist
+
+    from nanorts_b200.bots import Bot, Duel
+    from nanorts_b200.env import make
+    from nanorts_b200.sharding import EpisodeStats, Shard, shard_keys
+
+    game = scenario("duel")
+    env = make("NanoRTS", scenario=game, final_observation=False, device=device)
+    duel = Duel(env, tuple(Bot(f"player_{p}", s, t) for p, (s, t) in enumerate(DUEL_BOTS)))
+    L = args.lanes
+    shard = Shard(rank, world, world * L)
+    rng = np.random.default_rng(1234)
+    all_keys = torch.from_numpy(rng.integers(0, 2**32, size=(world * L, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
+    ds = duel.reset(shard_keys(all_keys, shard).to(device).view(torch.uint32))
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        duel.step(ds)
+    torch.cuda.synchronize(device)
+    step_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for i in range(args.steps):
+            step_events[i][0].record(stream)
+            duel.step(ds)
+            step_events[i][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    elapsed_ms = start.elapsed_time(end)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in step_events) / args.steps
+
+    stats = EpisodeStats(device)
+    for _ in range(args.stat_steps):
+        _, _, dones, infos = duel.step(ds)
+        stats.add_step(dones["__all__"], infos["winner"], infos["telemetry"].spawn_overflow)
+    episode_stats = stats.reduce()
+    timing = torch.tensor([elapsed_ms, kernel_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(timing, op=dist.ReduceOp.MAX)
+    elapsed_ms, kernel_ms = timing.tolist()
+
+    # End to end through the public API: each step launches the duel and reads
+    # the rewards, dones and winners back into pinned host memory.
+    host_rewards = torch.empty((L, 2), dtype=torch.float32).pin_memory()
+    host_dones = torch.empty((L,), dtype=torch.bool).pin_memory()
+    host_winner = torch.empty((L,), dtype=torch.int32).pin_memory()
+
+    def e2e_step() -> None:
+        _, rewards, dones, infos = duel.step(ds)
+        host_rewards.copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
+        host_dones.copy_(dones["__all__"], non_blocking=True)
+        host_winner.copy_(infos["winner"], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = max(float(e2e_ms.item()), 1e-9)
+
+    bytes_per = duel_algorithmic_bytes(game)
+    peak, peak_kind = load_peaks()
+    achieved = bytes_per["total"] * L / (kernel_ms * 1e-3) / 1e9
+    traffic = load_traffic("duel")
+    if traffic is not None:
+        traffic *= L
+    if rank == 0:
+        line = {
+            "metric": DUEL_METRIC,
+            "value": world * L * args.steps / (elapsed_ms * 1e-3),
+            "unit": "env-steps/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"{MAP} {UTT} {DUEL_STRATEGY}, player_0 WorkerRush vs player_1 LightRush, "
+                            "every game from its reset, auto-reset, max_cycles 5000",
+                "games_per_gpu": L,
+                "global_games": world * L,
+                "parallelism": f"dp{world} (independent games per GPU)",
+                "step": "nrts_duel_step (both bots, core step, auto-reset of State and carries)",
+                "l2": f"inputs larger than L2 (per-GPU working set {bytes_per['total'] * L / 2e6:.0f} MB read + written)",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": traffic,
+                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/duel_kernel_16x16.md)",
+                "algorithmic_bytes_per_launch": bytes_per["total"] * L,
+                "kernel": "nrts::duel_kernel",
+                "kernel_ms": kernel_ms,
+                "bytes_per_env_step": bytes_per["total"],
+                "peak_kind": peak_kind,
+                "note": "latency-bound (serial A* walks, low occupancy); the HBM fraction is reported, not a target",
+            },
+            "clocks": clocks.summary(),
+            "e2e": {
+                "value": world * L * args.e2e_steps / (e2e_ms * 1e-3),
+                "unit": "env-steps/s",
+                "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": world * L * (2 * 4 + 1 + 4),
+            },
+            "gpu_launches": args.steps,
+            "episodes": episode_stats,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = duel_cpu_baseline(game)
         print(json.dumps(line))
     if world > 1:
         dist.barrier()
