@@ -131,6 +131,10 @@ typedef struct NrtsOutputs {
     int32_t* sampled_actions[2];
     uint64_t sample_seed;
     uint64_t sample_counter;
+    /* Optional reward components float [L, 2, 6] of each step
+     * (adapters/rewards.py:20-72): win_loss, resource_gather, produce_worker,
+     * produce_building, attack, produce_combat_unit; needs the 7 standard unit types. */
+    float* reward_components;
 } NrtsOutputs;
 
 /* One environment step for every game: decode the action rows, the core step

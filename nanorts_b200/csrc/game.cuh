@@ -60,7 +60,7 @@ struct Layout {
     int32_t info_off;    // ReqInfo [2C]
     int32_t rank_off;    // int16 [2C] admission rank of each owned slot's request (-1 none)
     int32_t serial_off;  // int16 [2C] ranks of the contested requests
-    int32_t count_off;   // uint8 [cells rounded to 4] claims per cell, then 2 x uint32 produce claims
+    int32_t count_off;   // uint8 [cells rounded to 4] claims per cell, 2 x uint32 produce claims, 2 x 5 int32 reward-component counts
     // Completion scratch (aliases admission scratch).
     int32_t ret_off;     // Retained [2C]
     // Epilogue scratch (aliases both).

@@ -153,19 +153,29 @@ __device__ __forceinline__ void assign_pending(Game& g, int32_t slot, int32_t ki
     g.pending_order[slot] = order;
 }
 
+constexpr int kEventCounts = 5;
+
+// One admitted request's share of the reward components: kind is the kind
+// after the legality and blocking checks (admission.py:273-296).
+__device__ __forceinline__ void count_event(const Params& P, const Game& g, int32_t* ev, int32_t player, int32_t kind,
+                                            int32_t ptype, int32_t target) {
+    if (kind == kKindHarvest || kind == kKindReturn) {
+        atomicAdd(&ev[0], 1);
+    } else if (kind == kKindProduce) {
+        const int32_t t = clampi(ptype, 0, P.types - 1);
+        if (t == 3) atomicAdd(&ev[1], 1);                      // TYPE_WORKER
+        if (t == 1 || t == 2) atomicAdd(&ev[2], 1);            // TYPE_BASE, TYPE_BARRACKS
+        if (t == 4 || t == 5 || t == 6) atomicAdd(&ev[4], 1);  // TYPE_LIGHT, TYPE_HEAVY, TYPE_RANGED
+    } else if (kind == kKindAttack) {
+        const int32_t occupant = g.entity_at[clampi(target, 0, P.cells - 1)];
+        const int32_t owner = occupant == kAbsent ? kAbsent : g.owner[clampi(occupant, 0, P.entities - 1)];
+        if (owner == 1 - player) atomicAdd(&ev[3], 1);
+        else if (owner == player) atomicAdd(&ev[3], -1);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Admission (admission.py:48-156, reservations.py:69-306).
-//
-// Requests whose outcome cannot depend on another request are decided and
-// assigned by the lanes in parallel: a request meets a conflict only through a
-// pending holder that claims the same cell (MOVE and PRODUCE claim) or, for a
-// PRODUCE, a same-player PRODUCE holder whose cost with its own exceeds the
-// balance.  Requests claiming a cell that some other holder or request also
-// claims, and PRODUCE requests of a player with several PRODUCE claims, run
-// in Java order through the conflict resolution; the holders they can meet
-// are the claim holders of the step's start and the contested requests already
-// admitted.  A request whose own cost exceeds the balance conflicts with every
-// holder (reservations.py:122-135) and scans every slot.
 // ---------------------------------------------------------------------------
 // The contested requests in Java order: conflict resolution against the claim
 // holders (reservations.py:69-306), then the pending assignment.  `holders`
@@ -333,7 +343,12 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
     const int32_t count_words = (G.cells + 3) >> 2;
     uint32_t* produce_claims = counts + count_words;
 
-    for (int32_t i = lane; i < count_words + 2; i += 32) counts[i] = 0u;
+    // Reward-component counts (admission.py:273-296 as adapters/rewards.py:47-72
+    // combines them), per player: gathered, workers, buildings, attacks on the
+    // opponent minus attacks on own units, combat units.
+    int32_t* events = reinterpret_cast<int32_t*>(produce_claims + 2);
+    const bool counting = P.out.reward_components != nullptr;
+    for (int32_t i = lane; i < count_words + 2 + 2 * kEventCounts; i += 32) counts[i] = 0u;
     __syncwarp();
     // One pass over the slots: available owned slots (actions.py:65-75,
     // legality.py:169-170) and the claim holders at the step's start, with
@@ -389,6 +404,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                 }
                 if (claims_kind(kind)) add_claim(counts, G.cells, pos);
                 if (kind == kKindProduce) atomicAdd(&produce_claims[player], 1u);
+                if (counting) count_event(P, g, events + player * kEventCounts, player, kind, cptype, target);
                 ReqInfo r;
                 r.requested = requested;
                 r.none = none;
@@ -439,6 +455,10 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         R += __popc(__ballot_sync(kFull, issued));
     }
     __syncwarp();
+    if (counting && lane < 2 * kEventCounts) {
+        const int32_t player = lane / kEventCounts, c = lane % kEventCounts;
+        P.out.reward_components[(game * kPlayers + player) * 6 + 1 + c] = static_cast<float>(events[lane]);
+    }
     // Java order (admission.py:67-101): player, then rank or birth.
     {
         for (int32_t i = lane; i < A; i += 32) {

@@ -71,6 +71,11 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
         if (o.truncated) o.truncated[game] = truncated;
         if (o.winner) o.winner[game] = winner;
         if (o.spawn_overflow) reinterpret_cast<int2*>(o.spawn_overflow)[game] = make_int2(g.s[kSOverflow0], g.s[kSOverflow1]);
+        if (o.reward_components) {  // win_loss (adapters/rewards.py:51-53): decided games only, not truncated ones
+            const bool over = g.s[kSGameOver] != 0;
+            o.reward_components[game * 12] = over ? (winner == 0 ? 1.f : -1.f) : 0.f;
+            o.reward_components[game * 12 + 6] = over ? (winner == 1 ? 1.f : -1.f) : 0.f;
+        }
     }
     if (P.out.final_feature_maps[0] || P.out.final_feature_maps[1] || P.out.final_scalars[0] || P.out.final_scalars[1]) {
         uint8_t* const no_masks[2] = {nullptr, nullptr};
@@ -346,7 +351,7 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     L.info_off = U + round16(owned * 4);
     L.rank_off = L.info_off + round16(owned * 16);
     L.count_off = L.rank_off + round16(owned * 2);
-    const int32_t end_admission = L.count_off + round16(((cells + 3) / 4) * 4 + 8);
+    const int32_t end_admission = L.count_off + round16(((cells + 3) / 4) * 4 + 8 + 2 * 5 * 4);
     L.ret_off = U + round16(owned * 4);
     const int32_t end_completion = L.ret_off + round16(owned * 20);
     L.word_off = U;
@@ -539,6 +544,8 @@ int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const Nrts
     if (outputs == nullptr) return fail(NRTS_E_ARGUMENT, "outputs is null");
     if ((outputs->sampled_actions[0] == nullptr) != (outputs->sampled_actions[1] == nullptr))
         return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
+    if (outputs->reward_components != nullptr && extents->types < 7)
+        return fail(NRTS_E_ARGUMENT, "reward components need the seven standard unit types");
     P.mode = kModeStep;
     P.actions[0] = actions0;
     P.actions[1] = actions1;
@@ -594,6 +601,8 @@ int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const
     if (outputs == nullptr) return fail(NRTS_E_ARGUMENT, "outputs is null");
     if ((outputs->sampled_actions[0] == nullptr) != (outputs->sampled_actions[1] == nullptr))
         return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
+    if (outputs->reward_components != nullptr && extents->types < 7)
+        return fail(NRTS_E_ARGUMENT, "reward components need the seven standard unit types");
     P.mode = kModeDuel;
     P.bot[0] = bots[0];
     P.bot[1] = bots[1];

@@ -186,8 +186,10 @@ class NanoRTS:
             raise ModelError(f"NanoRTS refuses surface={surface!r}: this build publishes the symbolic surface only")
         if not isinstance(partial_observability, bool) or not isinstance(final_observation, bool):
             raise ModelError("partial_observability and final_observation must be bools")
-        if reward_components:
-            raise ModelError("NanoRTS refuses reward_components=True: the shaped reward components are not built here")
+        if not isinstance(reward_components, bool):
+            raise ModelError(f"NanoRTS refuses reward_components={reward_components!r}: it must be a bool")
+        if reward_components and scenario.bucket.unit_type_capacity < 7:
+            raise ModelError("reward_components needs the seven standard unit types (adapters/rewards.py:8-27)")
         if feature_dtype is None:
             feature_dtype = torch.uint8
         if feature_dtype not in (torch.uint8, torch.int16, torch.int32):
@@ -204,6 +206,7 @@ class NanoRTS:
         self.agents = list(AGENTS)
         self.num_agents = PLAYER_COUNT
         self.final_observation = final_observation
+        self.reward_components = reward_components
         self.partial_observability = partial_observability
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         widths = (ACTION_KIND_COUNT, DIRECTION_COUNT, DIRECTION_COUNT, DIRECTION_COUNT, DIRECTION_COUNT,
@@ -264,6 +267,8 @@ class NanoRTS:
         if self.final_observation:
             buf["final_feature_maps"] = torch.empty_like(buf["feature_maps"])
             buf["final_scalars"] = torch.empty_like(buf["scalars"])
+        if self.reward_components:
+            buf["reward_components"] = torch.empty((L, PLAYER_COUNT, 6), dtype=torch.float32, device=dev)
         state._buffers = buf
         return buf
 
@@ -347,6 +352,8 @@ class NanoRTS:
                 out.final_scalars[p] = _ptr(buf["final_scalars"][p])
         for name in ("reward", "done", "terminated", "truncated", "winner", "spawn_overflow"):
             setattr(out, name, _ptr(buf[name]))
+        if self.reward_components:
+            out.reward_components = _ptr(buf["reward_components"])
         sampled = None
         if sample is not None:
             # Two action buffers alternate so the draw never overwrites the rows this step reads.
@@ -370,6 +377,8 @@ class NanoRTS:
         }
         if self.final_observation:
             infos["final_observation"] = self._observations(buf, "final_")
+        if self.reward_components:  # facade.py:220-223, adapters/rewards.py:20-27 order
+            infos["reward_components"] = {agent: buf["reward_components"][:, p] for p, agent in enumerate(self.agents)}
         if sampled is not None:
             infos["sampled_actions"] = {agent: sampled[p] for p, agent in enumerate(self.agents)}
         return self._observations(buf), state, rewards, dones, infos

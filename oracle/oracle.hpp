@@ -307,6 +307,15 @@ struct Step {
 
     std::vector<int32_t> ranking;  // pending.ranking: slot at each pending rank
 
+    // StepEvents admission counts (model/step.py:24-33, admission.py:273-296):
+    // requests per player whose kind after the legality and blocking checks is
+    // HARVEST, RETURN, PRODUCE (by clipped produced type) or ATTACK (by the
+    // owner + 1 of the target cell's occupant, -1 for none).
+    int32_t admitted_harvest[kPlayers] = {0, 0};
+    int32_t admitted_return[kPlayers] = {0, 0};
+    int32_t admitted_attack[kPlayers][kPlayers + 1] = {{0, 0, 0}, {0, 0, 0}};
+    std::vector<int32_t> admitted_produce = std::vector<int32_t>(kPlayers * 8, 0);
+
     // admission.py:67-101 _ordered_requests.
     void ordered_requests(std::vector<int32_t>& order, std::vector<uint8_t>& issued_sorted, int32_t& issued_count) {
         const int32_t owned = x.owned();
@@ -467,6 +476,16 @@ struct Step {
             kind = kKindNone;
             none_duration = requested;
         }
+        if (issued) {  // _count_admitted (admission.py:273-307)
+            if (kind == kKindHarvest) ++admitted_harvest[player];
+            if (kind == kKindReturn) ++admitted_return[player];
+            if (kind == kKindProduce) ++admitted_produce[player * 8 + clip(cptype, 0, x.types - 1)];
+            if (kind == kKindAttack) {
+                const int32_t occupant = g.entity_at[clip(ctarget, 0, x.cells() - 1)];
+                const int32_t owner = occupant == kAbsent ? kAbsent : g.owner[clip(occupant, 0, x.entities() - 1)];
+                if (owner >= -1 && owner <= 1) ++admitted_attack[player][owner + 1];
+            }
+        }
         const Reservation request = reservation(c, x, g.cell[slot], g.owner[slot], kind, cdir, cptype, issued);
         resolve(slot, request, requested, kind, none_duration);
         const int32_t duration = kind == kKindNone ? none_duration : requested;
@@ -620,7 +639,11 @@ inline void decide(Game& g, const Extents& x) {
 struct StepOutcome {
     bool terminated, truncated;
     float reward[kPlayers];
+    float components[kPlayers][6];  // encode_components (adapters/rewards.py:47-72)
 };
+
+constexpr int kTypeBaseIdx = 1, kTypeBarracksIdx = 2, kTypeWorkerIdx = 3, kTypeLightIdx = 4, kTypeHeavyIdx = 5,
+              kTypeRangedIdx = 6;
 
 // core/__init__.py:99-110 _t1_step.
 inline StepOutcome core_step(Game& g, const Content& c, const Extents& x, const Commands& cmd, Key key) {
@@ -634,6 +657,18 @@ inline StepOutcome core_step(Game& g, const Content& c, const Extents& x, const 
     out.truncated = !*g.game_over && *g.time >= x.max_cycles;  // outcome.py:28-29
     const bool ended = out.terminated || out.truncated;
     for (int p = 0; p < kPlayers; ++p) out.reward[p] = ended ? (p == *g.winner ? 1.0f : -1.0f) : 0.0f;
+    // adapters/rewards.py:47-72 (order: win_loss, resource_gather, produce_worker,
+    // produce_building, attack, produce_combat_unit).
+    for (int p = 0; p < kPlayers; ++p) {
+        const int opponent = (p + 1) % kPlayers;
+        const int32_t* produced = &step.admitted_produce[p * 8];
+        out.components[p][0] = *g.game_over ? (*g.winner == p ? 1.0f : -1.0f) : 0.0f;
+        out.components[p][1] = static_cast<float>(step.admitted_harvest[p] + step.admitted_return[p]);
+        out.components[p][2] = static_cast<float>(produced[kTypeWorkerIdx]);
+        out.components[p][3] = static_cast<float>(produced[kTypeBaseIdx] + produced[kTypeBarracksIdx]);
+        out.components[p][4] = static_cast<float>(step.admitted_attack[p][opponent + 1] - step.admitted_attack[p][p + 1]);
+        out.components[p][5] = static_cast<float>(produced[kTypeLightIdx] + produced[kTypeHeavyIdx] + produced[kTypeRangedIdx]);
+    }
     return out;
 }
 

@@ -105,7 +105,7 @@ def _load() -> ctypes.CDLL:
         build()
     lib = ctypes.CDLL(str(LIBRARY))
     p = ctypes.c_void_p
-    lib.oracle_env_step.argtypes = [p, p, ctypes.c_int64] + [p] * 16 + [ctypes.c_int]
+    lib.oracle_env_step.argtypes = [p, p, ctypes.c_int64] + [p] * 17 + [ctypes.c_int]
     lib.oracle_core_step.argtypes = [p, p, ctypes.c_int64, p, p, p, p, p, ctypes.c_int]
     lib.oracle_legal_masks.argtypes = [p, p, ctypes.c_int64, p, p, ctypes.c_int]
     lib.oracle_observe.argtypes = [p, p, ctypes.c_int64, p, p, p, p, ctypes.c_int]
@@ -148,12 +148,13 @@ class Oracle:
     """Batch of L games stepped by the CPU restatement."""
 
     def __init__(self, game: GameConfig, lanes: int, *, partial_observability: bool = False,
-                 final_observation: bool = False, threads: int = 0) -> None:
+                 final_observation: bool = False, reward_components: bool = False, threads: int = 0) -> None:
         if game.bucket.index_dtype != np.int16:
             raise ValueError("the oracle handles int16 cell/slot indices only")
         self.game, self.lanes, self.threads = game, lanes, threads
         self.partial = partial_observability
         self.final_observation = final_observation
+        self.reward_components = reward_components
         b = game.bucket
         self.capacity, self.cells, self.mask_width = b.per_player_capacity, b.cell_count, b.mask_width
         self._reset = {k: np.ascontiguousarray(v) for k, v in reset_state(game).items()}
@@ -220,6 +221,8 @@ class Oracle:
             "spawn_overflow": np.empty((L, 2), np.int32),
         }
         final = self.final_observation
+        if self.reward_components:
+            out["reward_components"] = np.empty((L, 2, 6), np.float32)
         if final:
             out["final_fm"] = [np.empty((L, b.height, b.width, 6), np.uint8) for _ in range(2)]
             out["final_sc"] = [np.empty((L, 4), np.int32) for _ in range(2)]
@@ -231,6 +234,7 @@ class Oracle:
             _ptr(out["spawn_overflow"]),
             _ptr(out["final_fm"][0]) if final else None, _ptr(out["final_fm"][1]) if final else None,
             _ptr(out["final_sc"][0]) if final else None, _ptr(out["final_sc"][1]) if final else None,
+            _ptr(out["reward_components"]) if self.reward_components else None,
             self.threads,
         )
         assert rc == 0, rc
@@ -244,6 +248,8 @@ class Oracle:
             "winner": out["winner"],
             "spawn_overflow": out["spawn_overflow"],
         }
+        if self.reward_components:
+            result["reward_components"] = out["reward_components"]
         if final:
             result["final_feature_maps"] = np.stack(out["final_fm"], 1)
             result["final_scalars"] = np.stack(out["final_sc"], 1)

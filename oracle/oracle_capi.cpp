@@ -136,11 +136,12 @@ static Key episode_root(const OracleStates* s, int64_t lane) {
 
 // The JaxMARL step (adapters/jaxmarl/env.py:72-75 step = transition + respond):
 // decode -> core.step -> lifecycle.advance (auto-reset) -> observe the carried state.
-// `final_*` (may be null) receive observe(next_state) before the reset (env.py:161-170).
+// `final_*` (may be null) receive observe(next_state) before the reset (env.py:161-170);
+// `components` (may be null) receives the reward components [L, 2, 6] (env.py:173-174).
 int oracle_env_step(const OracleConfig* c, OracleStates* s, int64_t lanes, const int32_t* actions0, const int32_t* actions1,
                     uint8_t* fm0, uint8_t* fm1, int32_t* sc0, int32_t* sc1, float* reward, uint8_t* done, uint8_t* terminated,
                     uint8_t* truncated, int32_t* winner, int32_t* spawn_overflow, uint8_t* final_fm0, uint8_t* final_fm1,
-                    int32_t* final_sc0, int32_t* final_sc1, int threads) {
+                    int32_t* final_sc0, int32_t* final_sc1, float* components, int threads) {
     if (int e = check(c)) return e;
     set_threads(threads);
     const Extents x = extents_of(c);
@@ -162,6 +163,7 @@ int oracle_env_step(const OracleConfig* c, OracleStates* s, int64_t lanes, const
         winner[lane] = *g.winner;
         spawn_overflow[2 * lane] = g.spawn_overflow[0];
         spawn_overflow[2 * lane + 1] = g.spawn_overflow[1];
+        if (components != nullptr) std::memcpy(components + lane * 12, out.components, sizeof(out.components));
         if (final_fm0 != nullptr) {
             uint8_t* maps[kPlayers] = {final_fm0 + lane * cells * 6, final_fm1 + lane * cells * 6};
             int32_t* scalars[kPlayers] = {final_sc0 + lane * 4, final_sc1 + lane * 4};

@@ -67,14 +67,16 @@ def compare_masks(env, env_state, orc, where: str) -> np.ndarray:
 
 
 def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycles: int | None = None,
-               move_bias: float = 0.0, final_observation: bool = True) -> dict:
+               move_bias: float = 0.0, final_observation: bool = True, reward_components: bool = False) -> dict:
     from nanorts_b200.env import make
     from oracle.oracle import Oracle
 
     cfg = CONFIGS[config_name]
     game = cfg.game(max_cycles)
-    env = make("NanoRTS", scenario=game, partial_observability=cfg.partial, final_observation=final_observation)
-    orc = Oracle(game, lanes, partial_observability=cfg.partial, final_observation=final_observation)
+    env = make("NanoRTS", scenario=game, partial_observability=cfg.partial, final_observation=final_observation,
+               reward_components=reward_components)
+    orc = Oracle(game, lanes, partial_observability=cfg.partial, final_observation=final_observation,
+                 reward_components=reward_components)
     rng = np.random.default_rng(seed)
     keys = random_keys(rng, lanes)
     obs, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
@@ -82,6 +84,7 @@ def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycle
     compare_state(state, orc, "reset")
     compare_obs(obs, want_obs, "reset")
     episodes = 0
+    nonzero = {"any": 0, "attack": 0, "win_loss": 0}
     for t in range(steps):
         masks = compare_masks(env, state, orc, f"step {t} masks")
         actions = sample(masks, rng, move_bias)
@@ -100,8 +103,18 @@ def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycle
         assert np.array_equal(_np(infos["truncated"]), want["truncated"]), f"{where}: truncated"
         assert np.array_equal(_np(infos["winner"]), want["winner"]), f"{where}: winner"
         assert np.array_equal(_np(infos["telemetry"].spawn_overflow), want["spawn_overflow"]), f"{where}: overflow"
+        if reward_components:
+            for p, agent in enumerate(("player_0", "player_1")):
+                got = _np(infos["reward_components"][agent])
+                if not np.array_equal(got, want["reward_components"][:, p]):
+                    bad = np.argwhere(got != want["reward_components"][:, p])[:5]
+                    raise AssertionError(f"{where}: reward_components of {agent} differ at {bad.tolist()}")
+            nonzero["any"] += int(np.count_nonzero(want["reward_components"][..., 1:]))
+            nonzero["attack"] += int(np.count_nonzero(want["reward_components"][..., 4]))
+            nonzero["win_loss"] += int(np.count_nonzero(want["reward_components"][..., 0]))
         episodes += int(want["done"].sum())
-    return {"episodes": episodes, "time": orc.state["time"].copy(), "alt": orc.state["alternating_conflict_count"].copy()}
+    return {"episodes": episodes, "time": orc.state["time"].copy(), "alt": orc.state["alternating_conflict_count"].copy(),
+            "components": nonzero}
 
 
 @pytest.mark.parametrize("config_name", ["c1_8x8_both", "c2_16x16_random", "c3_16x16_alternating_partial"])
@@ -125,6 +138,15 @@ def test_parity_garden_of_war():
 def test_parity_long_horizon():
     """Games that run long enough for units to fight and die (default horizon)."""
     run_parity("c2_16x16_random", lanes=48, steps=1200, seed=11, final_observation=False)
+
+
+@pytest.mark.parametrize("config_name", ["c2_16x16_random", "c1_8x8_both"])
+def test_parity_reward_components(config_name):
+    """reward_components=True (adapters/rewards.py:47-72): every component of
+    both players at every step, over games long enough to fight and end."""
+    stats = run_parity(config_name, lanes=64, steps=700, seed=13, move_bias=0.3, final_observation=False,
+                       reward_components=True)
+    assert stats["components"]["any"] > 0 and stats["components"]["attack"] > 0
 
 
 def test_fused_sampler_matches_standalone_and_oracle():

@@ -236,3 +236,38 @@ def test_down_is_plus_width():
     orc.core_step(CommandSheet(game).set(0, 0, "move", direction=DOWN).array, np.zeros((1, 2), np.uint32))
     run_idle(orc, game, 9)
     assert orc.state["cell"][0, 0] == 2 * 4 + 1
+
+
+def test_reward_components_count_admitted_requests(oracle_lib):
+    """adapters/rewards.py:47-72 over admission.py:273-296 counts: one harvest,
+    one worker produced and one attack on the opponent for player 0; nothing
+    for player 1; win_loss 0 while the game runs."""
+    import numpy as np
+
+    from tests.helpers import tiny_game
+
+    game = tiny_game([("Resource", -1, 0, 1, 1, 10), ("Worker", 0, 1, 1, 1, 0), ("Base", 0, 3, 3, 10, 0),
+                      ("Light", 0, 4, 0, 4, 0), ("Worker", 1, 5, 0, 1, 0), ("Base", 1, 5, 5, 10, 0)],
+                     width=6, height=6, resources=(10, 10))
+    orc = oracle_lib.Oracle(game, 1, reward_components=True)
+    orc.reset(np.zeros((1, 2), np.uint32))
+    C = game.bucket.per_player_capacity
+    N = game.bucket.neutral_capacity
+    actions = np.zeros((1, 2, C, 7), np.int32)
+    actions[..., 0] = 0
+    types = orc.state["unit_type"][0]
+    owner = orc.state["owner"][0]
+    for s in range(N, N + C):
+        if owner[s] != 0:
+            continue
+        local = s - N
+        if types[s] == 3:  # worker: harvest the pile to its left
+            actions[0, 0, local] = [2, 0, 3, 0, 0, 0, 0]
+        elif types[s] == 1:  # base: produce a worker downwards
+            actions[0, 0, local] = [4, 0, 0, 0, 2, 3, 0]
+        elif types[s] == 4:  # light: attack the enemy worker one cell right
+            actions[0, 0, local] = [5, 0, 0, 0, 0, 0, 3 * 7 + 4]
+    out = orc.step(actions)
+    comp = out["reward_components"][0]
+    assert comp[0].tolist() == [0.0, 1.0, 1.0, 0.0, 1.0, 0.0]
+    assert comp[1].tolist() == [0.0] * 6
