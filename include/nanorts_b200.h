@@ -28,6 +28,8 @@
  *                      assembly, as called by NanoRTS.step (adapters/jaxmarl/facade.py:107-119)
  *   nrts_reset         NanoRTS.reset (adapters/jaxmarl/facade.py:100-105)
  *   nrts_legal_masks   NanoRTS.get_avail_actions (facade.py:172-174 -> core/cuda/legality.cu)
+ *   nrts_packed_masks  jaxmarl.legal_actions with mask_form="packed" (adapters/jaxmarl/actions.py:28-41,
+ *                      adapters/factors.py:89-103)
  *   nrts_observe       NanoRTS.get_obs (facade.py:166-170 -> observations/cuda/visibility.cu)
  *   nrts_slot_cells    NanoRTS.get_slot_cells (facade.py:176-178)
  *   nrts_bot_act       XLA FFI target nanorts_abstraction_act (bots/cuda/abstraction_act.cu:1099-1322),
@@ -135,6 +137,11 @@ typedef struct NrtsOutputs {
      * (adapters/rewards.py:20-72): win_loss, resource_gather, produce_worker,
      * produce_building, attack, produce_combat_unit; needs the 7 standard unit types. */
     float* reward_components;
+    /* Optional legality rows in the packed form uint32 [L, C, 3] per player
+     * (mask_form="packed", adapters/factors.py:89-103): word 0 holds the
+     * 6+16+T kind, direction and produce-type bits, words 1 and 2 the attack
+     * window's bits 0-31 and 32-63. */
+    uint32_t* packed_masks[2];
 } NrtsOutputs;
 
 /* One environment step for every game: decode the action rows, the core step
@@ -153,6 +160,12 @@ int nrts_reset(const NrtsExtents* extents, const NrtsContent* content, const Nrt
 /* Legality rows of the current state (get_avail_actions, facade.py:172-174). */
 int nrts_legal_masks(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
                      uint8_t* masks0, uint8_t* masks1, void* stream);
+
+/* Legality rows of the current state in the packed form (see
+ * NrtsOutputs.packed_masks): jaxmarl.legal_actions with mask_form="packed"
+ * (adapters/jaxmarl/actions.py:28-41). */
+int nrts_packed_masks(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
+                      uint32_t* words0, uint32_t* words1, void* stream);
 
 /* Observations of the current state (get_obs, facade.py:166-170). */
 int nrts_observe(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,

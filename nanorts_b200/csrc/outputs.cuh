@@ -185,6 +185,22 @@ __device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game,
     }
 }
 
+// One player's legality rows in the packed form (adapters/factors.py:89-103):
+// word 0 = the first 6+16+T bits, words 1-2 = the attack window's bits.
+__device__ void write_packed(const Params& P, const uint32_t* rows, int64_t game, uint32_t* out, int lane) {
+    const int32_t head = P.mask_width - P.offsets;
+    const uint32_t head_mask = (1u << head) - 1u;
+    const uint32_t hi_mask = P.offsets > 32 ? ((P.offsets >= 64) ? ~0u : ((1u << (P.offsets - 32)) - 1u)) : 0u;
+    const uint32_t lo_mask = P.offsets >= 32 ? ~0u : ((1u << P.offsets) - 1u);
+    uint32_t* base = out + game * static_cast<int64_t>(P.capacity) * 3;
+    for (int32_t r = lane; r < P.capacity; r += 32) {
+        const uint32_t w0 = rows[3 * r], w1 = rows[3 * r + 1], w2 = rows[3 * r + 2];
+        base[3 * r] = w0 & head_mask;
+        base[3 * r + 1] = __funnelshift_r(w0, w1, head) & lo_mask;
+        base[3 * r + 2] = __funnelshift_r(w1, w2, head) & hi_mask;
+    }
+}
+
 // Feature bytes [hp, carried, owner (1 self, 2 opponent), type+1, pending, terrain]
 // of a cell word seen by `player`, as the low four bytes and the high two.
 __device__ __forceinline__ void features(uint32_t w, int player, bool shown, uint32_t& lo, uint32_t& hi) {
@@ -349,7 +365,8 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
     uint64_t* occ = reinterpret_cast<uint64_t*>(slab + L.rows_off);
     uint64_t* vis = occ + 2 * G.h;
     uint32_t* rows = reinterpret_cast<uint32_t*>(slab + L.mask_off);
-    const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample;
+    const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample || P.out.packed_masks[0] != nullptr ||
+                            P.out.packed_masks[1] != nullptr;
     const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
     cell_words(H, G, g, words, occ, want_masks, lane);
     if (want_masks) {
@@ -402,6 +419,8 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
         __syncwarp();
         for (int player = 0; player < kPlayers; ++player) {
             if (masks[player] != nullptr) write_masks(P, rows + player * P.capacity * 3, game, masks[player], lane);
+            if (P.out.packed_masks[player] != nullptr)
+                write_packed(P, rows + player * P.capacity * 3, game, P.out.packed_masks[player], lane);
         }
     }
     if (want_obs) {

@@ -193,7 +193,8 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
     }
     store_bots(P, slab, game, lane);
     const NrtsOutputs& o = P.out;
-    if (o.masks[0] || o.masks[1] || o.feature_maps[0] || o.feature_maps[1] || o.scalars[0] || o.scalars[1] || P.sampled[0])
+    if (o.masks[0] || o.masks[1] || o.packed_masks[0] || o.packed_masks[1] || o.feature_maps[0] || o.feature_maps[1] ||
+        o.scalars[0] || o.scalars[1] || P.sampled[0])
         write_outputs(P, H, G, g, slab, game, o.masks, o.feature_maps, o.scalars, P.sampled[0] != nullptr, lane);
     finish_bot_stores();
     __syncwarp();
@@ -515,6 +516,14 @@ int launch_step(Params& P, void* stream) {
     return NRTS_OK;
 }
 
+// factors.refuse_mask_form (adapters/factors.py:63-86): the packed words hold
+// the non-attack groups in one word and the attack window in two.
+int check_packable(const NrtsExtents* x) {
+    if (kKinds + 4 * kDirections + x->types > 32) return fail(NRTS_E_ARGUMENT, "packed masks need 6+16+T <= 32 bits in word 0");
+    if (x->offsets > 64) return fail(NRTS_E_ARGUMENT, "packed masks need an attack window of at most 64 cells");
+    return NRTS_OK;
+}
+
 int check_bot(const NrtsExtents* x, const NrtsContent* content, const NrtsBot* bot) {
     if (bot == nullptr) return fail(NRTS_E_ARGUMENT, "bot is null");
     for (int t = 0; t < x->types; ++t) {
@@ -546,6 +555,8 @@ int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const Nrts
         return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
     if (outputs->reward_components != nullptr && extents->types < 7)
         return fail(NRTS_E_ARGUMENT, "reward components need the seven standard unit types");
+    if (outputs->packed_masks[0] != nullptr || outputs->packed_masks[1] != nullptr)
+        if (int rc = check_packable(extents)) return rc;
     P.mode = kModeStep;
     P.actions[0] = actions0;
     P.actions[1] = actions1;
@@ -566,8 +577,11 @@ int nrts_reset(const NrtsExtents* extents, const NrtsContent* content, const Nrt
     if (outputs != nullptr) {
         if ((outputs->sampled_actions[0] == nullptr) != (outputs->sampled_actions[1] == nullptr))
             return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
+        if (outputs->packed_masks[0] != nullptr || outputs->packed_masks[1] != nullptr)
+            if (int rc = check_packable(extents)) return rc;
         for (int p = 0; p < kPlayers; ++p) {
             P.out.masks[p] = outputs->masks[p];
+            P.out.packed_masks[p] = outputs->packed_masks[p];
             P.out.feature_maps[p] = outputs->feature_maps[p];
             P.out.scalars[p] = outputs->scalars[p];
             P.sampled[p] = outputs->sampled_actions[p];
@@ -620,6 +634,17 @@ int nrts_legal_masks(const NrtsExtents* extents, const NrtsContent* content, con
     P.mode = kModeOutputs;
     P.out.masks[0] = masks0;
     P.out.masks[1] = masks1;
+    return launch_step(P, stream);
+}
+
+int nrts_packed_masks(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes, uint32_t* words0,
+                      uint32_t* words1, void* stream) {
+    Params P;
+    if (int rc = fill_params(P, extents, content, state, lanes)) return rc;
+    if (int rc = check_packable(extents)) return rc;
+    P.mode = kModeOutputs;
+    P.out.packed_masks[0] = words0;
+    P.out.packed_masks[1] = words1;
     return launch_step(P, stream);
 }
 

@@ -44,6 +44,8 @@ ALL_AGENTS = "__all__"
 ENVIRONMENT_IDS = ("NanoRTS",)
 ACTION_FACTORS = ("kind", "move_direction", "harvest_direction", "return_direction", "produce_direction",
                   "produce_type", "attack_offset")
+MASK_FORMS = ("rows", "packed")  # adapters/factors.py:23
+MASK_WORDS = 3
 NONE_DURATION = 1
 
 LEAVES = (
@@ -139,6 +141,7 @@ class JaxMARLLayout:
     mask_offsets: tuple[int, ...]
     mask_width: int
     feature_maps_dtype: torch.dtype
+    mask_form: str = "rows"
 
     @property
     def agents(self) -> tuple[str, ...]:
@@ -154,19 +157,22 @@ class JaxMARLLayout:
 
     @property
     def mask_shape(self) -> tuple[int, int]:
-        return (self.per_player_capacity, self.mask_width)
+        """layout.py:64-67: rows, or the three factor-aligned words of the packed form."""
+        return (self.per_player_capacity, self.mask_width if self.mask_form == "rows" else MASK_WORDS)
 
 
 def make(env_id: str, *, scenario: GameConfig, utt: UnitTypeTableVersion | None = None, surface: str = "symbolic",
          partial_observability: bool = False, final_observation: bool = True, feature_dtype: Any = None,
-         reward_components: bool = False, device: Any = None) -> NanoRTS:
-    """``nanorts.make`` (adapters/jaxmarl/facade.py:43-56)."""
+         reward_components: bool = False, device: Any = None, mask_form: str = "rows") -> NanoRTS:
+    """``nanorts.make`` (adapters/jaxmarl/facade.py:43-56).  ``mask_form`` is
+    ``jaxmarl.prepare``'s (adapters/jaxmarl/layout.py:70-95): ``"packed"`` makes
+    ``get_avail_actions`` return uint32 [L, C, 3] words (adapters/factors.py:89-103)."""
     if env_id not in ENVIRONMENT_IDS:
         raise ModelError(f"make refuses environment id {env_id!r}: the accepted ids are {list(ENVIRONMENT_IDS)}")
     game = scenario if utt is None else _content.with_unit_type_table(scenario, utt)
     return NanoRTS(game, surface=surface, partial_observability=partial_observability,
                    final_observation=final_observation, feature_dtype=feature_dtype,
-                   reward_components=reward_components, device=device)
+                   reward_components=reward_components, device=device, mask_form=mask_form)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -181,7 +187,7 @@ class NanoRTS:
 
     def __init__(self, scenario: GameConfig, *, surface: str = "symbolic", partial_observability: bool = False,
                  final_observation: bool = True, feature_dtype: Any = None, reward_components: bool = False,
-                 device: Any = None) -> None:
+                 device: Any = None, mask_form: str = "rows") -> None:
         if surface != "symbolic":
             raise ModelError(f"NanoRTS refuses surface={surface!r}: this build publishes the symbolic surface only")
         if not isinstance(partial_observability, bool) or not isinstance(final_observation, bool):
@@ -195,6 +201,12 @@ class NanoRTS:
         if feature_dtype not in (torch.uint8, torch.int16, torch.int32):
             raise ModelError(f"feature_dtype {feature_dtype!r} is none of uint8, int16, int32")
         bucket = scenario.bucket
+        if mask_form not in MASK_FORMS:
+            raise ModelError(f"NanoRTS refuses mask_form={mask_form!r}: a mask publishes one of {list(MASK_FORMS)}")
+        if mask_form == "packed" and (ACTION_KIND_COUNT + 4 * DIRECTION_COUNT + bucket.unit_type_capacity > 32
+                                      or bucket.attack_offset_capacity > 64):
+            raise ModelError("mask_form='packed' needs 6+16+T <= 32 and an attack window of at most 64 cells "
+                             "(adapters/factors.py:63-86)")
         if bucket.index_dtype != np.int16:
             raise ModelError("this build steps scenarios whose cell and slot indices fit int16")
         if bucket.width > 64 or bucket.height > 64:
@@ -216,7 +228,9 @@ class NanoRTS:
             height=bucket.height, width=bucket.width, per_player_capacity=bucket.per_player_capacity,
             surface=surface, partial_observability=partial_observability, final_observation=final_observation,
             action_widths=widths, mask_offsets=offsets, mask_width=sum(widths), feature_maps_dtype=feature_dtype,
+            mask_form=mask_form,
         )
+        self.packed = mask_form == "packed"
         self._shapes = leaf_shapes(bucket)
         self._extents = Extents(
             height=bucket.height, width=bucket.width, neutral=bucket.neutral_capacity,
@@ -253,8 +267,12 @@ class NanoRTS:
             return state._buffers
         L, b, dev = state.lanes, self.game.bucket, self.device
         u8 = torch.uint8
+        mask_buffer = (("packed_masks", torch.empty((PLAYER_COUNT, L, b.per_player_capacity, MASK_WORDS), dtype=torch.uint32,
+                                                    device=dev)) if self.packed else
+                       ("masks", torch.empty((PLAYER_COUNT, L, b.per_player_capacity, self.layout.mask_width), dtype=u8,
+                                             device=dev)))
         buf = {
-            "masks": torch.empty((PLAYER_COUNT, L, b.per_player_capacity, self.layout.mask_width), dtype=u8, device=dev),
+            mask_buffer[0]: mask_buffer[1],
             "feature_maps": torch.empty((PLAYER_COUNT, L, b.height, b.width, 6), dtype=u8, device=dev),
             "scalars": torch.empty((PLAYER_COUNT, L, 4), dtype=torch.int32, device=dev),
             "reward": torch.empty((L, PLAYER_COUNT), dtype=torch.float32, device=dev),
@@ -314,7 +332,7 @@ class NanoRTS:
         state = self._empty_state(int(key.shape[0]))
         buf = self._buffers(state)
         out = Outputs()
-        out.masks[0], out.masks[1] = _ptr(buf["masks"][0]), _ptr(buf["masks"][1])
+        self._set_masks(out, buf)
         out.feature_maps[0], out.feature_maps[1] = _ptr(buf["feature_maps"][0]), _ptr(buf["feature_maps"][1])
         out.scalars[0], out.scalars[1] = _ptr(buf["scalars"][0]), _ptr(buf["scalars"][1])
         ptrs = self._state_ptrs(state)
@@ -343,8 +361,8 @@ class NanoRTS:
                 raise ModelError(f"actions[{agent!r}] must be a contiguous int32 tensor [L, {C}, 7] on {self.device}")
             rows.append(a)
         out = Outputs()
+        self._set_masks(out, buf)
         for p in range(PLAYER_COUNT):
-            out.masks[p] = _ptr(buf["masks"][p])
             out.feature_maps[p] = _ptr(buf["feature_maps"][p])
             out.scalars[p] = _ptr(buf["scalars"][p])
             if self.final_observation:
@@ -383,15 +401,42 @@ class NanoRTS:
             infos["sampled_actions"] = {agent: sampled[p] for p, agent in enumerate(self.agents)}
         return self._observations(buf), state, rewards, dones, infos
 
+    def _set_masks(self, out: Outputs, buf: dict[str, torch.Tensor]) -> None:
+        name = "packed_masks" if self.packed else "masks"
+        target = out.packed_masks if self.packed else out.masks
+        target[0], target[1] = _ptr(buf[name][0]), _ptr(buf[name][1])
+
     def get_avail_actions(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
-        """bool[L, C, 78] per agent (facade.py:172-174); reuses the rows the last step wrote."""
+        """bool[L, C, 78] per agent (facade.py:172-174), or uint32[L, C, 3] words with
+        mask_form="packed"; reuses what the last step wrote."""
         buf = self._buffers(state)
+        if self.packed:
+            if not state._masks_current:
+                ptrs = self._state_ptrs(state)
+                check(library().nrts_packed_masks(ctypes.byref(self._extents), ctypes.byref(self._content),
+                                                  ctypes.byref(ptrs), state.lanes, _ptr(buf["packed_masks"][0]),
+                                                  _ptr(buf["packed_masks"][1]), self._stream()))
+                state._masks_current = True
+            return {agent: buf["packed_masks"][p] for p, agent in enumerate(self.agents)}
         if not state._masks_current:
             ptrs = self._state_ptrs(state)
             check(library().nrts_legal_masks(ctypes.byref(self._extents), ctypes.byref(self._content),
                                              ctypes.byref(ptrs), state.lanes, _ptr(buf["masks"][0]),
                                              _ptr(buf["masks"][1]), self._stream()))
             state._masks_current = True
+        return {agent: buf["masks"][p].view(torch.bool) for p, agent in enumerate(self.agents)}
+
+    def _row_masks(self, state: EnvironmentState) -> dict[str, torch.Tensor]:
+        """Byte rows of the current state whatever the mask form (the standalone sampler reads rows)."""
+        if not self.packed:
+            return self.get_avail_actions(state)
+        buf = self._buffers(state)
+        if "masks" not in buf:
+            buf["masks"] = torch.empty((PLAYER_COUNT, state.lanes, self.game.bucket.per_player_capacity,
+                                        self.layout.mask_width), dtype=torch.uint8, device=self.device)
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_legal_masks(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs),
+                                         state.lanes, _ptr(buf["masks"][0]), _ptr(buf["masks"][1]), self._stream()))
         return {agent: buf["masks"][p].view(torch.bool) for p, agent in enumerate(self.agents)}
 
     def invalidate(self, state: EnvironmentState) -> None:
@@ -418,7 +463,7 @@ class NanoRTS:
     def sample_actions(self, state: EnvironmentState, seed: int, counter: int) -> dict[str, torch.Tensor]:
         """Uniform legal actions per factor from the current masks (the rollout stand-in for
         per-factor categorical sampling over masked logits, README.md:53-63)."""
-        masks = self.get_avail_actions(state)
+        masks = self._row_masks(state)
         acts = self._action_buffer(state)
         check(library().nrts_sample_actions(ctypes.byref(self._extents), state.lanes, _ptr(masks["player_0"]),
                                             _ptr(masks["player_1"]), _ptr(acts[0]), _ptr(acts[1]),
@@ -440,3 +485,13 @@ class NanoRTS:
         row = torch.zeros(self.layout.mask_width, dtype=torch.bool)
         row[self.layout.mask_offsets[0] + KIND_NONE] = True
         return row
+
+
+def unpack_mask(words: torch.Tensor, layout: JaxMARLLayout) -> torch.Tensor:
+    """adapters/factors.py:106-114 unpack: packed uint32 [..., 3] words -> bool [..., 78] rows."""
+    if layout.mask_form != "packed":
+        return words
+    head = sum(layout.action_widths[:-1])
+    shifts = torch.arange(32, device=words.device, dtype=torch.int64)
+    bits = ((words.to(torch.int64)[..., None] >> shifts) & 1).bool().reshape(*words.shape[:-1], MASK_WORDS * 32)
+    return torch.cat([bits[..., :head], bits[..., 32:32 + layout.action_widths[-1]]], dim=-1)

@@ -58,7 +58,7 @@ class Outputs(ctypes.Structure):
         ("truncated", ctypes.c_void_p), ("winner", ctypes.c_void_p), ("spawn_overflow", ctypes.c_void_p),
         ("final_feature_maps", ctypes.c_void_p * 2), ("final_scalars", ctypes.c_void_p * 2),
         ("sampled_actions", ctypes.c_void_p * 2), ("sample_seed", ctypes.c_uint64), ("sample_counter", ctypes.c_uint64),
-        ("reward_components", ctypes.c_void_p),
+        ("reward_components", ctypes.c_void_p), ("packed_masks", ctypes.c_void_p * 2),
     ]
 
 
@@ -76,7 +76,8 @@ class BotSpec(ctypes.Structure):
 
 # Every symbol the header declares.
 SYMBOLS = (
-    "nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells", "nrts_sample_actions",
+    "nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
+    "nrts_slot_cells", "nrts_sample_actions",
     "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
 )
 
@@ -99,6 +100,7 @@ def library() -> ctypes.CDLL:
     lib.nrts_step.argtypes = [p, p, p, i64, p, p, p, p]
     lib.nrts_reset.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_legal_masks.argtypes = [p, p, p, i64, p, p, p]
+    lib.nrts_packed_masks.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_observe.argtypes = [p, p, p, i64, p, p, p, p, p]
     lib.nrts_slot_cells.argtypes = [p, p, i64, p, p]
     lib.nrts_sample_actions.argtypes = [p, i64, p, p, p, p, ctypes.c_uint64, ctypes.c_uint64, p]
@@ -108,7 +110,8 @@ def library() -> ctypes.CDLL:
     lib.nrts_self_check.argtypes = [p, i64]
     lib.nrts_build_id.restype = ctypes.c_char_p
     lib.nrts_last_error.restype = ctypes.c_char_p
-    for name in ("nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_observe", "nrts_slot_cells",
+    for name in ("nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
+                 "nrts_slot_cells",
                  "nrts_sample_actions", "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_self_check"):
         getattr(lib, name).restype = i32
     _LIB = lib

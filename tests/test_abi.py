@@ -154,3 +154,4 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(runtime, "_LIB", None)
     with pytest.raises(runtime.KernelUnavailable):
         runtime.library()
+

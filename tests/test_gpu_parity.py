@@ -178,3 +178,51 @@ def test_fused_sampler_matches_standalone_and_oracle():
         for a in fused:
             assert torch.equal(fused[a], standalone[a]), f"step {t}: fused draw differs for {a}"
         actions = fused
+
+
+def pack_rows(rows: np.ndarray, widths: tuple[int, ...]) -> np.ndarray:
+    """adapters/factors.py:89-103 pack, on uint8 [..., 78] rows."""
+    head = sum(widths[:-1])
+    middle = head + min(widths[-1], 32)
+    words = []
+    for start, stop in ((0, head), (head, middle), (middle, head + widths[-1])):
+        shifts = np.arange(stop - start, dtype=np.uint64)
+        words.append((rows[..., start:stop].astype(np.uint64) << shifts).sum(-1).astype(np.uint32))
+    return np.stack(words, -1)
+
+
+@pytest.mark.parametrize("config_name", ["c2_16x16_random", "c5_64x64_random"])
+def test_packed_masks_match_the_oracle_rows(config_name):
+    """mask_form='packed': the step's packed words, nrts_packed_masks on a
+    state it did not produce, and their unpacking all equal the oracle's rows."""
+    from nanorts_b200.env import make, unpack_mask
+    from oracle.oracle import Oracle
+
+    cfg = CONFIGS[config_name]
+    game = cfg.game(100)
+    lanes = 32 if config_name.startswith("c2") else 6
+    env = make("NanoRTS", scenario=game, final_observation=False, mask_form="packed")
+    assert env.layout.mask_shape == (game.bucket.per_player_capacity, 3)
+    orc = Oracle(game, lanes)
+    rng = np.random.default_rng(21)
+    keys = random_keys(rng, lanes)
+    _, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
+    orc.reset(keys)
+    widths = env.layout.action_widths
+    for t in range(150):
+        want_rows = orc.legal_masks()
+        words = env.get_avail_actions(state)
+        for p, agent in enumerate(("player_0", "player_1")):
+            got = words[agent].view(torch.int32).cpu().numpy().view(np.uint32)
+            assert np.array_equal(got, pack_rows(want_rows[:, p], widths)), f"step {t}: packed words of {agent}"
+            assert np.array_equal(unpack_mask(words[agent], env.layout).cpu().numpy(), want_rows[:, p].astype(bool))
+        if t % 25 == 0:  # the standalone entry point on the same state
+            env.invalidate(state)
+            again = env.get_avail_actions(state)
+            for agent in again:
+                assert torch.equal(again[agent], words[agent].clone()), f"step {t}: nrts_packed_masks differs"
+        actions = sample(want_rows, rng, 0.3)
+        orc.step(actions)
+        acts = {f"player_{p}": torch.from_numpy(np.ascontiguousarray(actions[:, p])).cuda() for p in range(2)}
+        env.step(None, state, acts)
+        compare_state(state, orc, f"packed step {t}")
