@@ -26,6 +26,9 @@
  *                      nanorts_visible_cells (observations/cuda/visibility.cu) plus
  *                      the XLA fusions of decode_actions, observe and mask
  *                      assembly, as called by NanoRTS.step (adapters/jaxmarl/facade.py:107-119)
+ *   nrts_step_groups   the XLA FFI target nanorts_step_groups that core.step_groups calls
+ *                      (core/__init__.py:63-89, core/cuda/step.cu:390-405) for GroupMix
+ *                      (bots/mix.py:107-160): one launch over several groups of games
  *   nrts_reset         NanoRTS.reset (adapters/jaxmarl/facade.py:100-105)
  *   nrts_legal_masks   NanoRTS.get_avail_actions (facade.py:172-174 -> core/cuda/legality.cu)
  *   nrts_packed_masks  jaxmarl.legal_actions with mask_form="packed" (adapters/jaxmarl/actions.py:28-41,
@@ -150,6 +153,24 @@ typedef struct NrtsOutputs {
  * Replaces NanoRTS.step (adapters/jaxmarl/facade.py:107-119). */
 int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes,
               const int32_t* actions0, const int32_t* actions1, const NrtsOutputs* outputs, void* stream);
+
+/* One group of a multi-group step: its own content (map, unit table, reset
+ * State), State buffers, lane count, action rows and outputs.  Every group's
+ * extents must equal the first group's except max_cycles. */
+#define NRTS_MAX_GROUPS 8
+typedef struct NrtsGroupStep {
+    const NrtsExtents* extents;
+    const NrtsContent* content;
+    const NrtsState* state;
+    int64_t lanes;
+    const int32_t* actions[2];
+    const NrtsOutputs* outputs;
+} NrtsGroupStep;
+
+/* nrts_step for up to NRTS_MAX_GROUPS groups of games in one launch
+ * (core.step_groups, core/__init__.py:63-89, as GroupMix steps groups that
+ * share a bucket, bots/mix.py:130-160). */
+int nrts_step_groups(const NrtsGroupStep* groups, int32_t count, void* stream);
 
 /* Every game to its reset State with episode 0 and the given root keys
  * ([L, 2] uint32, may alias state->environment_root); writes masks and

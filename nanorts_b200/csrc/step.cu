@@ -124,10 +124,10 @@ __device__ __forceinline__ bool run_game(const Params& P, const Header& H, const
     return true;
 }
 
-// Each warp steps the games blockIdx * warps + warp + k * (all warps); the
+// Each warp steps the games block * warps + warp + k * (blocks * warps); the
 // launch gives every game its own warp.
 template <int kW>
-__global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Params P) {
+__device__ __forceinline__ void step_block(const Params& P, int64_t block, int64_t blocks) {
     extern __shared__ __align__(128) char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -142,12 +142,33 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Pa
         fence_mbar_init();
     }
     __syncthreads();
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * warps;
+    const int64_t stride = blocks * warps;
     uint32_t parity = 0;
-    for (int64_t game = static_cast<int64_t>(blockIdx.x) * warps + warp; game < P.lanes; game += stride) {
+    for (int64_t game = block * warps + warp; game < P.lanes; game += stride) {
         if (!run_game(P, H, G, slab, bar, parity, game, lane)) break;
         if (P.mode != kModeReset) parity ^= 1u;
     }
+}
+
+template <int kW>
+__global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Params P) {
+    step_block<kW>(P, blockIdx.x, gridDim.x);
+}
+
+// Several groups of games in one launch: the CTAs of group k are the blocks
+// [block_start[k], block_start[k + 1]), each group with its own Params.
+constexpr int kMaxGroups = NRTS_MAX_GROUPS;
+struct GroupParams {
+    int32_t count;
+    int32_t block_start[kMaxGroups + 1];
+    Params group[kMaxGroups];
+};
+
+template <int kW>
+__global__ void __launch_bounds__(256, 3) groups_kernel(const __grid_constant__ GroupParams GP) {
+    int k = 0;
+    while (k + 1 < GP.count && static_cast<int32_t>(blockIdx.x) >= GP.block_start[k + 1]) ++k;
+    step_block<kW>(GP.group[k], static_cast<int64_t>(blockIdx.x) - GP.block_start[k], GP.block_start[k + 1] - GP.block_start[k]);
 }
 
 // One game of a bot launch.  Bot-act: the bot of P.bot_player chooses that
@@ -382,6 +403,16 @@ struct DeviceInfo {
 
 DeviceInfo g_devices[64];
 
+const void* pick_groups_kernel(int width) {
+    switch (width) {
+        case 8: return reinterpret_cast<const void*>(groups_kernel<8>);
+        case 16: return reinterpret_cast<const void*>(groups_kernel<16>);
+        case 32: return reinterpret_cast<const void*>(groups_kernel<32>);
+        case 64: return reinterpret_cast<const void*>(groups_kernel<64>);
+        default: return reinterpret_cast<const void*>(groups_kernel<0>);
+    }
+}
+
 const void* pick_kernel(int width, bool bots = false) {
     if (bots) {
         switch (width) {
@@ -413,6 +444,8 @@ int prepare_device(int& device, DeviceInfo*& info) {
                 if (cudaFuncSetAttribute(pick_kernel(w, bots), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                     return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(step/duel kernel) failed");
             }
+            if (cudaFuncSetAttribute(pick_groups_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(groups kernel) failed");
         }
         info->ready = true;
     }
@@ -469,6 +502,25 @@ template <int kW>
 void launch_instance(const Params& P, unsigned blocks, int threads, size_t smem, cudaStream_t stream) {
     if (P.mode == kModeDuel || P.mode == kModeBotAct) duel_kernel<kW><<<blocks, threads, smem, stream>>>(P);
     else step_kernel<kW><<<blocks, threads, smem, stream>>>(P);
+}
+
+// Warps per CTA with the most games resident per SM (registers and shared
+// memory), fewer when the batch would not fill every SM twice.
+int choose_warps(const void* kernel, const Layout& L, int64_t lanes, const DeviceInfo* info) {
+    int best_warps = 1, best_resident = 0;
+    for (int warps = 1; warps <= 8; ++warps) {
+        const size_t smem = L.header_bytes + static_cast<size_t>(warps) * L.slab_bytes;
+        if (smem > static_cast<size_t>(info->smem_optin)) break;
+        int blocks = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, warps * 32, smem) != cudaSuccess) continue;
+        if (blocks * warps >= best_resident) {
+            best_resident = blocks * warps;
+            best_warps = warps;
+        }
+    }
+    int warps = best_warps;
+    while (warps > 1 && (lanes + warps - 1) / warps < 2 * info->sms) --warps;
+    return warps;
 }
 
 int launch_step(Params& P, void* stream) {
@@ -565,6 +617,73 @@ int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const Nrts
     P.sampled[1] = outputs->sampled_actions[1];
     P.sample_key = sample_key(outputs->sample_seed, outputs->sample_counter);
     return launch_step(P, stream);
+}
+
+int nrts_step_groups(const NrtsGroupStep* groups, int32_t count, void* stream) {
+    if (groups == nullptr) return fail(NRTS_E_ARGUMENT, "groups is null");
+    if (count < 1 || count > kMaxGroups) return fail(NRTS_E_ARGUMENT, "between 1 and 8 groups per launch");
+    static thread_local GroupParams GP;
+    std::memset(&GP, 0, sizeof(GP));
+    const NrtsExtents* x0 = groups[0].extents;
+    if (x0 == nullptr) return fail(NRTS_E_ARGUMENT, "a group's extents is null");
+    bool aligned = true;
+    int64_t total = 0;
+    for (int k = 0; k < count; ++k) {
+        const NrtsGroupStep& gs = groups[k];
+        const NrtsExtents* x = gs.extents;
+        if (x == nullptr) return fail(NRTS_E_ARGUMENT, "a group's extents is null");
+        if (x->height != x0->height || x->width != x0->width || x->neutral != x0->neutral || x->capacity != x0->capacity ||
+            x->types != x0->types || x->offsets != x0->offsets || x->strategy != x0->strategy ||
+            x->partial_observability != x0->partial_observability)
+            return fail(NRTS_E_ARGUMENT, "groups of one launch must share their extents (all but max_cycles)");
+        Params& P = GP.group[k];
+        if (int rc = fill_params(P, x, gs.content, gs.state, gs.lanes)) return rc;
+        if (gs.actions[0] == nullptr || gs.actions[1] == nullptr) return fail(NRTS_E_ARGUMENT, "a group's actions are null");
+        if (gs.outputs == nullptr) return fail(NRTS_E_ARGUMENT, "a group's outputs is null");
+        const NrtsOutputs* o = gs.outputs;
+        if ((o->sampled_actions[0] == nullptr) != (o->sampled_actions[1] == nullptr))
+            return fail(NRTS_E_ARGUMENT, "sampled_actions needs both players' buffers or neither");
+        if (o->reward_components != nullptr && x->types < 7)
+            return fail(NRTS_E_ARGUMENT, "reward components need the seven standard unit types");
+        P.mode = kModeStep;
+        P.actions[0] = gs.actions[0];
+        P.actions[1] = gs.actions[1];
+        P.out = *o;
+        P.sampled[0] = o->sampled_actions[0];
+        P.sampled[1] = o->sampled_actions[1];
+        P.sample_key = sample_key(o->sample_seed, o->sample_counter);
+        aligned &= P.layout.aligned != 0;
+        total += gs.lanes;
+    }
+    // One slab layout for every CTA of the launch.
+    const Layout common = make_layout(x0, aligned, false);
+    for (int k = 0; k < count; ++k) GP.group[k].layout = common;
+    int device;
+    DeviceInfo* info;
+    if (int rc = prepare_device(device, info)) return rc;
+    if (total == 0) return NRTS_OK;
+    if (common.header_bytes + common.slab_bytes > info->smem_optin) return fail(NRTS_E_ARGUMENT, "one game does not fit in shared memory");
+    const int warps = choose_warps(pick_groups_kernel(x0->width), common, total, info);
+    GP.count = count;
+    GP.block_start[0] = 0;
+    for (int k = 0; k < count; ++k) {
+        const int64_t blocks = (GP.group[k].lanes + warps - 1) / warps;
+        if (GP.block_start[k] + blocks > INT32_MAX) return fail(NRTS_E_ARGUMENT, "too many games for one launch");
+        GP.block_start[k + 1] = GP.block_start[k] + static_cast<int32_t>(blocks);
+    }
+    const size_t smem = common.header_bytes + static_cast<size_t>(warps) * common.slab_bytes;
+    const unsigned blocks = static_cast<unsigned>(GP.block_start[count]);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (x0->width) {
+        case 8: groups_kernel<8><<<blocks, warps * 32, smem, s>>>(GP); break;
+        case 16: groups_kernel<16><<<blocks, warps * 32, smem, s>>>(GP); break;
+        case 32: groups_kernel<32><<<blocks, warps * 32, smem, s>>>(GP); break;
+        case 64: groups_kernel<64><<<blocks, warps * 32, smem, s>>>(GP); break;
+        default: groups_kernel<0><<<blocks, warps * 32, smem, s>>>(GP); break;
+    }
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("groups kernel launch: ") + cudaGetErrorString(err));
+    return NRTS_OK;
 }
 
 int nrts_reset(const NrtsExtents* extents, const NrtsContent* content, const NrtsState* state, int64_t lanes, const uint32_t* keys,
@@ -742,7 +861,8 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
         cudaFuncAttributes attributes;
         const void* kernels[] = {pick_kernel(8), pick_kernel(16), pick_kernel(32), pick_kernel(64), pick_kernel(7),
                                  pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
-                                 pick_kernel(7, true),
+                                 pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
+                                 pick_groups_kernel(64), pick_groups_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
                                  reinterpret_cast<const void*>(probe_kernel)};
         for (const void* k : kernels) {

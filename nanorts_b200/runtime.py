@@ -62,6 +62,13 @@ class Outputs(ctypes.Structure):
     ]
 
 
+class GroupStep(ctypes.Structure):
+    """NrtsGroupStep: one group of a multi-group step."""
+    _fields_ = [("extents", ctypes.c_void_p), ("content", ctypes.c_void_p), ("state", ctypes.c_void_p),
+                ("lanes", ctypes.c_int64), ("actions", ctypes.c_void_p * 2), ("outputs", ctypes.c_void_p)]
+
+
+MAX_GROUPS = 8
 CARRY_FIELDS = 9
 
 
@@ -76,7 +83,7 @@ class BotSpec(ctypes.Structure):
 
 # Every symbol the header declares.
 SYMBOLS = (
-    "nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
+    "nrts_prepare_scenario", "nrts_step", "nrts_step_groups", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
     "nrts_slot_cells", "nrts_sample_actions",
     "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
 )
@@ -99,6 +106,7 @@ def library() -> ctypes.CDLL:
     lib.nrts_prepare_scenario.argtypes = [p, p, p, p]
     lib.nrts_step.argtypes = [p, p, p, i64, p, p, p, p]
     lib.nrts_reset.argtypes = [p, p, p, i64, p, p, p]
+    lib.nrts_step_groups.argtypes = [p, i32, p]
     lib.nrts_legal_masks.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_packed_masks.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_observe.argtypes = [p, p, p, i64, p, p, p, p, p]
@@ -110,7 +118,7 @@ def library() -> ctypes.CDLL:
     lib.nrts_self_check.argtypes = [p, i64]
     lib.nrts_build_id.restype = ctypes.c_char_p
     lib.nrts_last_error.restype = ctypes.c_char_p
-    for name in ("nrts_prepare_scenario", "nrts_step", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
+    for name in ("nrts_prepare_scenario", "nrts_step", "nrts_step_groups", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
                  "nrts_slot_cells",
                  "nrts_sample_actions", "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_self_check"):
         getattr(lib, name).restype = i32
