@@ -145,6 +145,10 @@ typedef struct NrtsOutputs {
      * 6+16+T kind, direction and produce-type bits, words 1 and 2 the attack
      * window's bits 0-31 and 32-63. */
     uint32_t* packed_masks[2];
+    /* Scheduling hint: nonzero takes the games last to first.  Alternating it
+     * between consecutive steps of one batch lets the games the previous launch
+     * wrote last (still in L2) go first; results do not depend on it. */
+    uint32_t reverse_order;
 } NrtsOutputs;
 
 /* One environment step for every game: decode the action rows, the core step

@@ -145,6 +145,8 @@ class Duel:
                 out.masks[p] = _ptr(buf["masks"][p])
                 out.feature_maps[p] = _ptr(buf["feature_maps"][p])
                 out.scalars[p] = _ptr(buf["scalars"][p])
+        out.reverse_order = state._launches & 1
+        state._launches += 1
         specs = (BotSpec * PLAYER_COUNT)(*(_spec(b.strategy, b.trained, c) for b, c in zip(self.bots, duel.carries)))
         ptrs = env._state_ptrs(state)
         check(library().nrts_duel_step(ctypes.byref(env._extents), ctypes.byref(env._content), ctypes.byref(ptrs),

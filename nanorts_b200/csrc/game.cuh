@@ -96,6 +96,7 @@ struct Params {
     int32_t bot_player;     // bot-act: the acting player
     int32_t* commands;      // bot-act: Commands int32 [L, 6, 2, C]
     int32_t rank_bits;      // admission rank field width (admission.py:104-115)
+    int32_t reverse;        // take the games last to first (NrtsOutputs.reverse_order)
     Layout layout;
     NrtsScenario scenario;  // copied to shared memory by every CTA
 };

@@ -144,7 +144,8 @@ __device__ __forceinline__ void step_block(const Params& P, int64_t block, int64
     __syncthreads();
     const int64_t stride = blocks * warps;
     uint32_t parity = 0;
-    for (int64_t game = block * warps + warp; game < P.lanes; game += stride) {
+    for (int64_t g0 = block * warps + warp; g0 < P.lanes; g0 += stride) {
+        const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
         if (!run_game(P, H, G, slab, bar, parity, game, lane)) break;
         if (P.mode != kModeReset) parity ^= 1u;
     }
@@ -240,7 +241,8 @@ __global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Param
     __syncthreads();
     const int64_t stride = static_cast<int64_t>(gridDim.x) * warps;
     uint32_t parity = 0;
-    for (int64_t game = static_cast<int64_t>(blockIdx.x) * warps + warp; game < P.lanes; game += stride) {
+    for (int64_t g0 = static_cast<int64_t>(blockIdx.x) * warps + warp; g0 < P.lanes; g0 += stride) {
+        const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
         if (!run_bots(P, H, G, slab, bar, parity, game, lane)) break;
         parity ^= 1u;
     }
@@ -613,6 +615,7 @@ int nrts_step(const NrtsExtents* extents, const NrtsContent* content, const Nrts
     P.actions[0] = actions0;
     P.actions[1] = actions1;
     P.out = *outputs;
+    P.reverse = outputs->reverse_order != 0;
     P.sampled[0] = outputs->sampled_actions[0];
     P.sampled[1] = outputs->sampled_actions[1];
     P.sample_key = sample_key(outputs->sample_seed, outputs->sample_counter);
@@ -649,6 +652,7 @@ int nrts_step_groups(const NrtsGroupStep* groups, int32_t count, void* stream) {
         P.actions[0] = gs.actions[0];
         P.actions[1] = gs.actions[1];
         P.out = *o;
+        P.reverse = o->reverse_order != 0;
         P.sampled[0] = o->sampled_actions[0];
         P.sampled[1] = o->sampled_actions[1];
         P.sample_key = sample_key(o->sample_seed, o->sample_counter);
@@ -740,6 +744,7 @@ int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const
     P.bot[0] = bots[0];
     P.bot[1] = bots[1];
     P.out = *outputs;
+    P.reverse = outputs->reverse_order != 0;
     P.sampled[0] = outputs->sampled_actions[0];
     P.sampled[1] = outputs->sampled_actions[1];
     P.sample_key = sample_key(outputs->sample_seed, outputs->sample_counter);

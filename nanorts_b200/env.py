@@ -121,6 +121,7 @@ class EnvironmentState:
     episode_index: torch.Tensor     # uint32 [L]
     _buffers: dict[str, torch.Tensor] = dataclasses.field(default_factory=dict, repr=False)
     _masks_current: bool = dataclasses.field(default=False, repr=False)
+    _launches: int = dataclasses.field(default=0, repr=False)  # alternates the kernel's traversal order
 
     @property
     def lanes(self) -> int:
@@ -378,6 +379,8 @@ class NanoRTS:
             sampled = self._action_buffer(state, avoid=rows[0].data_ptr())
             out.sampled_actions[0], out.sampled_actions[1] = _ptr(sampled[0]), _ptr(sampled[1])
             out.sample_seed, out.sample_counter = sample[0] & (2**64 - 1), sample[1] & (2**64 - 1)
+        out.reverse_order = state._launches & 1
+        state._launches += 1
         ptrs = self._state_ptrs(state)
         check(library().nrts_step(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs), L,
                                   _ptr(rows[0]), _ptr(rows[1]), ctypes.byref(out), self._stream()))

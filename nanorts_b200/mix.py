@@ -176,6 +176,8 @@ class GroupMix:
                     setattr(out, field, _ptr(gbuf[field]))
                 if env.reward_components:
                     out.reward_components = _ptr(gbuf["reward_components"])
+                out.reverse_order = state._launches & 1
+                state._launches += 1
                 ptrs = env._state_ptrs(state)
                 keep.extend((out, ptrs))
                 table[j].extents = ctypes.addressof(env._extents)

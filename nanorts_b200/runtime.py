@@ -58,7 +58,7 @@ class Outputs(ctypes.Structure):
         ("truncated", ctypes.c_void_p), ("winner", ctypes.c_void_p), ("spawn_overflow", ctypes.c_void_p),
         ("final_feature_maps", ctypes.c_void_p * 2), ("final_scalars", ctypes.c_void_p * 2),
         ("sampled_actions", ctypes.c_void_p * 2), ("sample_seed", ctypes.c_uint64), ("sample_counter", ctypes.c_uint64),
-        ("reward_components", ctypes.c_void_p), ("packed_masks", ctypes.c_void_p * 2),
+        ("reward_components", ctypes.c_void_p), ("packed_masks", ctypes.c_void_p * 2), ("reverse_order", ctypes.c_uint32),
     ]
 
 
