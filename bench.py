@@ -38,15 +38,33 @@ DUEL_METRIC = "env steps/sec (bot vs bot: both bots' commands + core step + auto
 MAP, UTT, STRATEGY = "basesWorkers16x16", "VERSION_ORIGINAL", "CANCEL_RANDOM"
 DUEL_STRATEGY = "CANCEL_BOTH"
 DEFAULT_LANES = {"random": 16384, "duel": 32768}
+# BASELINE.json configs with uniform random legal actions (config 4 is the duel):
+# map, unit table, conflict strategy, partial observability, capacity profile,
+# games (per GPU, or in all for strong scaling), scaling.
+CONFIGS = {
+    1: ("basesWorkers8x8", "VERSION_ORIGINAL", "CANCEL_BOTH", False, True, 1024, "weak"),
+    2: ("basesWorkers16x16", "VERSION_ORIGINAL", "CANCEL_RANDOM", False, True, 16384, "weak"),
+    3: ("basesWorkers16x16", "VERSION_ORIGINAL_FINETUNED", "CANCEL_ALTERNATING", True, True, 65536, "strong"),
+    5: ("GardenOfWar64x64", "VERSION_ORIGINAL", "CANCEL_RANDOM", False, False, 4096, "weak"),
+}
 # family.py strategy numbers and trained types of WorkerRush (player 0) and LightRush (player 1).
 DUEL_BOTS = ((0, -1), (1, 4))
 
 
-def scenario(workload: str = "random"):
+def scenario(workload: str = "random", config: int = 2):
     from nanorts_b200 import map_name_to_scenario
 
-    strategy = DUEL_STRATEGY if workload == "duel" else STRATEGY
-    return map_name_to_scenario(MAP, utt=UTT, conflict_strategy=strategy, max_cycles=5000)
+    if workload == "duel":
+        return map_name_to_scenario(MAP, utt=UTT, conflict_strategy=DUEL_STRATEGY, max_cycles=5000)
+    name, utt, strategy, _, profile, _, _ = CONFIGS[config]
+    return map_name_to_scenario(name, utt=utt, conflict_strategy=strategy, max_cycles=5000, capacity_profile=profile)
+
+
+def workload_name(config: int) -> str:
+    name, utt, strategy, partial, profile, _, _ = CONFIGS[config]
+    obs = ", partial observability" if partial else ""
+    cap = "" if profile else ", capacity_profile=False"
+    return f"configs[{config - 1}]: {name} {utt} {strategy}{obs}{cap}, uniform random legal actions per factor, auto-reset"
 
 
 def duel_algorithmic_bytes(game) -> dict[str, int]:
@@ -163,13 +181,14 @@ class ClockSampler:
         }
 
 
-def cpu_baseline(game, seconds: float = 12.0, lanes: int = 512, threads: int | None = None) -> dict:
+def cpu_baseline(game, seconds: float = 12.0, lanes: int = 512, threads: int | None = None, partial: bool = False,
+                 label: str = f"{MAP}/{STRATEGY}") -> dict:
     """The CPU oracle (C++ restatement of the reference's JAX program path,
     OpenMP over games) on a bounded sample of the same workload."""
     from oracle.oracle import Oracle, sample_uniform_legal
 
     threads = threads or os.cpu_count() or 1
-    orc = Oracle(game, lanes, threads=threads)
+    orc = Oracle(game, lanes, threads=threads, partial_observability=partial)
     rng = np.random.default_rng(0)
     orc.reset(rng.integers(0, 2**32, size=(lanes, 2), dtype=np.uint64).astype(np.uint32))
     widths = (6, 4, 4, 4, 4, game.bucket.unit_type_capacity, game.bucket.attack_offset_capacity)
@@ -189,7 +208,7 @@ def cpu_baseline(game, seconds: float = 12.0, lanes: int = 512, threads: int | N
         "unit": "env-steps/s",
         "cores": threads,
         "kind": "port",
-        "sample": f"{lanes} games x {steps} steps of {MAP}/{STRATEGY}, C++ oracle step + masks + observations "
+        "sample": f"{lanes} games x {steps} steps of {label}, C++ oracle step + masks + observations "
                   f"(sampling excluded), {threads} OpenMP threads",
     }
 
@@ -262,12 +281,13 @@ def run_reference(args) -> None:
             "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }))
         return
-    game = scenario()
+    game = scenario(config=args.config)
+    partial = CONFIGS[args.config][3]
     from oracle.oracle import Oracle, sample_uniform_legal
 
     threads = os.cpu_count() or 1
-    lanes = 256
-    orc = Oracle(game, lanes, threads=threads)
+    lanes = 256 if args.config != 5 else 32
+    orc = Oracle(game, lanes, threads=threads, partial_observability=partial)
     rng = np.random.default_rng(0)
     orc.reset(rng.integers(0, 2**32, size=(lanes, 2), dtype=np.uint64).astype(np.uint32))
     widths = (6, 4, 4, 4, 4, game.bucket.unit_type_capacity, game.bucket.attack_offset_capacity)
@@ -285,10 +305,10 @@ def run_reference(args) -> None:
     line = {
         "impl": "reference",
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": CONFIGS[args.config][6],
         "vs_baseline": None, "dtype": "int32", "data": "synthetic",
-        "config": {"workload": f"{MAP} {UTT} {STRATEGY}, uniform legal actions, auto-reset",
-                   "lanes_per_step_sample": lanes, "full_lanes": args.lanes},
+        "config": {"workload": workload_name(args.config), "lanes_per_step_sample": lanes, "full_lanes": args.lanes},
         "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
                          "sample": f"{lanes} games per step on {threads} threads; the reference's JAX CPU path is not "
                                    "runnable here (jax absent, reference install failed), so its C++ restatement runs"},
@@ -303,7 +323,9 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=2000)
     parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--workload", default="random", choices=("random", "duel"),
-                        help="random: configs[1] (uniform legal actions); duel: configs[3] (WorkerRush vs LightRush)")
+                        help="random: uniform legal actions (configs 1, 2, 3, 5); duel: configs[3] (WorkerRush vs LightRush)")
+    parser.add_argument("--config", type=int, default=2, choices=(1, 2, 3, 4, 5),
+                        help="BASELINE.json config number (1-based); 2 is the headline, 4 selects the duel")
     parser.add_argument("--lanes", type=int, default=None, help="games per GPU")
     parser.add_argument("--impl", default="nanorts_b200", choices=("nanorts_b200", "reference"))
     parser.add_argument("--e2e-steps", type=int, default=50)
@@ -315,8 +337,10 @@ def main() -> None:
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
+    if args.config == 4:
+        args.workload = "duel"
     if args.lanes is None:
-        args.lanes = DEFAULT_LANES[args.workload]
+        args.lanes = DEFAULT_LANES["duel"] if args.workload == "duel" else CONFIGS[args.config][5]
     if args.stat_steps is None:
         args.stat_steps = 600 if args.workload == "duel" else 200
     if args.impl == "reference":
@@ -343,13 +367,16 @@ def main() -> None:
     if args.workload == "duel":
         run_duel(args, world, rank, local, device)
         return
-    game = scenario()
-    env = make("NanoRTS", scenario=game, final_observation=False, device=device)
-    L = args.lanes
-    # Weak scaling: world * L games, each rank steps its contiguous block of L.
-    shard = Shard(rank, world, world * L)
+    game = scenario(config=args.config)
+    partial, scaling = CONFIGS[args.config][3], CONFIGS[args.config][6]
+    env = make("NanoRTS", scenario=game, final_observation=False, device=device, partial_observability=partial)
+    # Weak scaling: world * lanes games, each rank steps its contiguous block of
+    # lanes; strong scaling (config 3): lanes games in all, split over the ranks.
+    global_games = args.lanes if scaling == "strong" else world * args.lanes
+    shard = Shard(rank, world, global_games)
+    L = shard.lanes
     rng = np.random.default_rng(1234)
-    all_keys = torch.from_numpy(rng.integers(0, 2**32, size=(world * L, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
+    all_keys = torch.from_numpy(rng.integers(0, 2**32, size=(global_games, 2), dtype=np.uint64).astype(np.uint32).view(np.int32))
     _, state = env.reset(shard_keys(all_keys, shard).to(device).view(torch.uint32))
     stream = torch.cuda.current_stream(device)
 
@@ -446,12 +473,12 @@ def main() -> None:
         bytes_per["total"] += bytes_per["sampled_actions"]
     peak, peak_kind = load_peaks()
     achieved = bytes_per["total"] * L / (step_kernel_ms * 1e-3) / 1e9
-    traffic = load_traffic()
+    traffic = load_traffic() if args.config == 2 else None
     if traffic is not None:  # ncu DRAM bytes per env-step -> per launch of L games
         traffic *= L
     line = None
     if rank == 0:
-        value = world * L * args.steps / (elapsed_ms * 1e-3)
+        value = global_games * args.steps / (elapsed_ms * 1e-3)
         line = {
             "metric": METRIC,
             "value": value,
@@ -461,14 +488,14 @@ def main() -> None:
             "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling,
             "vs_baseline": None,
             "dtype": "int32",
             "data": "synthetic",
             "config": {
-                "workload": f"{MAP} {UTT} {STRATEGY}, C=70, uniform random legal actions per factor, auto-reset",
+                "workload": workload_name(args.config),
                 "games_per_gpu": L,
-                "global_games": world * L,
+                "global_games": global_games,
                 "parallelism": f"dp{world} (independent games per GPU)",
                 "step": "nrts_sample_actions + nrts_step" if not fused else
                         "nrts_step with the fused uniform draw of the next actions",
@@ -491,16 +518,18 @@ def main() -> None:
             },
             "clocks": clocks.summary(),
             "e2e": {
-                "value": world * L * e2e_steps / (e2e_ms * 1e-3),
+                "value": global_games * e2e_steps / (e2e_ms * 1e-3),
                 "unit": "env-steps/s",
-                "h2d_bytes_per_step": world * L * C * 7 * 4 * 2,
-                "d2h_bytes_per_step": world * (L * C * 7 * 4 * 2 + L * 2 * 4 + L),
+                "h2d_bytes_per_step": global_games * C * 7 * 4 * 2,
+                "d2h_bytes_per_step": global_games * C * 7 * 4 * 2 + global_games * (2 * 4 + 1),
             },
             "gpu_launches": (1 if fused else 2) * args.steps,
             "episodes": episode_stats,
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(game)
+            name, _, strategy = CONFIGS[args.config][:3]
+            line["cpu_baseline"] = cpu_baseline(game, lanes=512 if args.config != 5 else 48, partial=partial,
+                                                label=f"{name}/{strategy}")
         print(json.dumps(line))
     if world > 1:
         dist.barrier()

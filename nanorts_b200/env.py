@@ -106,6 +106,46 @@ class State:
         return [getattr(self, name) for name in LEAVES]
 
 
+class StepInfos(dict):
+    """The step's infos; values are views of the state's output buffers that
+    the next step on the same state overwrites.  ``spawn_overflowed`` is
+    derived from the telemetry when first read after a step."""
+
+    def __init__(self, spawn_overflow: torch.Tensor) -> None:
+        super().__init__()
+        self._spawn_overflow = spawn_overflow
+
+    def stale(self) -> None:
+        super().pop("spawn_overflowed", None)
+
+    def _derive(self) -> None:
+        if not super().__contains__("spawn_overflowed"):
+            super().__setitem__("spawn_overflowed", (self._spawn_overflow > 0).any(dim=1))
+
+    def __getitem__(self, key):
+        if key == "spawn_overflowed":
+            self._derive()
+        return super().__getitem__(key)
+
+    def __contains__(self, key) -> bool:
+        return key == "spawn_overflowed" or super().__contains__(key)
+
+    def get(self, key, default=None):
+        return self[key] if key in self else default
+
+    def keys(self):
+        self._derive()
+        return super().keys()
+
+    def items(self):
+        self._derive()
+        return super().items()
+
+    def __iter__(self):
+        self._derive()
+        return super().__iter__()
+
+
 @dataclasses.dataclass
 class SymbolicObservation:
     feature_maps: torch.Tensor  # uint8 [L, H, W, 6]
@@ -122,6 +162,7 @@ class EnvironmentState:
     _buffers: dict[str, torch.Tensor] = dataclasses.field(default_factory=dict, repr=False)
     _masks_current: bool = dataclasses.field(default=False, repr=False)
     _launches: int = dataclasses.field(default=0, repr=False)  # alternates the kernel's traversal order
+    _cache: dict = dataclasses.field(default_factory=dict, repr=False)  # per-state call structures and views
 
     @property
     def lanes(self) -> int:
@@ -302,11 +343,17 @@ class NanoRTS:
         return second if in_first else first
 
     def _state_ptrs(self, state: EnvironmentState) -> StatePtrs:
+        leaves = state.core_state.leaves()
+        key = tuple(leaf.data_ptr() for leaf in leaves) + (state.environment_root.data_ptr(), state.episode_index.data_ptr())
+        cached = state._cache.get("ptrs")
+        if cached is not None and cached[0] == key:
+            return cached[1]
         ptrs = StatePtrs(environment_root=_ptr(state.environment_root), episode_index=_ptr(state.episode_index))
-        for k, leaf in enumerate(state.core_state.leaves()):
+        for k, leaf in enumerate(leaves):
             if leaf.device != self.device or not leaf.is_contiguous():
                 raise ModelError("every state leaf must be a contiguous tensor on the environment's device")
             ptrs.leaf[k] = leaf.data_ptr()
+        state._cache["ptrs"] = (key, ptrs)
         return ptrs
 
     def _stream(self) -> int:
@@ -361,6 +408,37 @@ class NanoRTS:
             if a.shape != (L, C, 7) or a.dtype != torch.int32 or a.device != self.device or not a.is_contiguous():
                 raise ModelError(f"actions[{agent!r}] must be a contiguous int32 tensor [L, {C}, 7] on {self.device}")
             rows.append(a)
+        call = state._cache.get("step")
+        if call is None:
+            call = self._step_call(state, buf)
+            state._cache["step"] = call
+        out, results = call["outputs"], call["results"]
+        infos = results[3]
+        if sample is not None:
+            # Two action buffers alternate so the draw never overwrites the rows this step reads.
+            sampled = self._action_buffer(state, avoid=rows[0].data_ptr())
+            out.sampled_actions[0], out.sampled_actions[1] = _ptr(sampled[0]), _ptr(sampled[1])
+            out.sample_seed, out.sample_counter = sample[0] & (2**64 - 1), sample[1] & (2**64 - 1)
+            infos["sampled_actions"] = {agent: sampled[p] for p, agent in enumerate(self.agents)}
+        else:
+            out.sampled_actions[0] = out.sampled_actions[1] = None
+            infos.pop("sampled_actions", None)
+        out.reverse_order = state._launches & 1
+        state._launches += 1
+        infos.stale()
+        ptrs = self._state_ptrs(state)
+        check(library().nrts_step(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs), L,
+                                  _ptr(rows[0]), _ptr(rows[1]), ctypes.byref(out), self._stream()))
+        state._masks_current = True
+        observations, rewards, dones = results[0], results[1], results[2]
+        if self.layout.feature_maps_dtype != torch.uint8:  # converted copies, not views: fresh every step
+            observations = self._observations(buf)
+            if self.final_observation:
+                infos["final_observation"] = self._observations(buf, "final_")
+        return observations, state, rewards, dones, infos
+
+    def _step_call(self, state: EnvironmentState, buf: dict[str, torch.Tensor]) -> dict:
+        """The Outputs struct and the returned views of one state's buffers, built once."""
         out = Outputs()
         self._set_masks(out, buf)
         for p in range(PLAYER_COUNT):
@@ -373,36 +451,22 @@ class NanoRTS:
             setattr(out, name, _ptr(buf[name]))
         if self.reward_components:
             out.reward_components = _ptr(buf["reward_components"])
-        sampled = None
-        if sample is not None:
-            # Two action buffers alternate so the draw never overwrites the rows this step reads.
-            sampled = self._action_buffer(state, avoid=rows[0].data_ptr())
-            out.sampled_actions[0], out.sampled_actions[1] = _ptr(sampled[0]), _ptr(sampled[1])
-            out.sample_seed, out.sample_counter = sample[0] & (2**64 - 1), sample[1] & (2**64 - 1)
-        out.reverse_order = state._launches & 1
-        state._launches += 1
-        ptrs = self._state_ptrs(state)
-        check(library().nrts_step(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs), L,
-                                  _ptr(rows[0]), _ptr(rows[1]), ctypes.byref(out), self._stream()))
-        state._masks_current = True
         done = buf["done"].view(torch.bool)
         rewards = {agent: buf["reward"][:, p] for p, agent in enumerate(self.agents)}
         dones = {agent: done for agent in self.agents} | {ALL_AGENTS: done}
-        infos: dict[str, Any] = {
+        infos = StepInfos(buf["spawn_overflow"])
+        infos.update({
             "terminated": buf["terminated"].view(torch.bool),
             "truncated": buf["truncated"].view(torch.bool),
             "winner": buf["winner"],
             "telemetry": Telemetry(spawn_overflow=buf["spawn_overflow"]),
-            "spawn_overflowed": (buf["spawn_overflow"] > 0).any(dim=1),
             "final_valid": done,
-        }
+        })
         if self.final_observation:
             infos["final_observation"] = self._observations(buf, "final_")
         if self.reward_components:  # facade.py:220-223, adapters/rewards.py:20-27 order
             infos["reward_components"] = {agent: buf["reward_components"][:, p] for p, agent in enumerate(self.agents)}
-        if sampled is not None:
-            infos["sampled_actions"] = {agent: sampled[p] for p, agent in enumerate(self.agents)}
-        return self._observations(buf), state, rewards, dones, infos
+        return {"outputs": out, "results": (self._observations(buf), rewards, dones, infos)}
 
     def _set_masks(self, out: Outputs, buf: dict[str, torch.Tensor]) -> None:
         name = "packed_masks" if self.packed else "masks"
