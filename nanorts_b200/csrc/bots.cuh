@@ -195,25 +195,6 @@ __device__ __forceinline__ bool bot_row(const Params& P, char* slab, int64_t gam
 
 constexpr int kBotRows = kSlabLeaves;
 
-// Copies n < 16 bytes; the loads all issue before the first store.
-__device__ __forceinline__ void copy_edge_in(char* dst, const char* src, uint32_t n) {
-    uint8_t b[15];
-#pragma unroll
-    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? __ldg(reinterpret_cast<const unsigned char*>(src) + i) : 0;
-#pragma unroll
-    for (uint32_t i = 0; i < 15; ++i)
-        if (i < n) dst[i] = static_cast<char>(b[i]);
-}
-
-__device__ __forceinline__ void copy_edge_out(char* dst, const char* src, uint32_t n) {
-    uint8_t b[15];
-#pragma unroll
-    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? static_cast<uint8_t>(src[i]) : 0;
-#pragma unroll
-    for (uint32_t i = 0; i < 15; ++i)
-        if (i < n) dst[i] = static_cast<char>(b[i]);
-}
-
 // State leaves -> slab in one mbarrier phase, carries while it is in flight.
 // Lane r owns row r: it issues the TMA bulk copy of the row's 16-byte-aligned
 // body and copies the unaligned head and tail bytes itself.

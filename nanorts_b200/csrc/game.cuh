@@ -285,6 +285,25 @@ __device__ bool wait_phase(uint64_t* bar, uint32_t parity) {
     return true;
 }
 
+// Copies n < 16 bytes; every load issues before the first store.
+__device__ __forceinline__ void copy_edge_in(char* dst, const char* src, uint32_t n) {
+    uint8_t b[15];
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? __ldg(reinterpret_cast<const unsigned char*>(src) + i) : 0;
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i)
+        if (i < n) dst[i] = static_cast<char>(b[i]);
+}
+
+__device__ __forceinline__ void copy_edge_out(char* dst, const char* src, uint32_t n) {
+    uint8_t b[15];
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i) b[i] = i < n ? static_cast<uint8_t>(src[i]) : 0;
+#pragma unroll
+    for (uint32_t i = 0; i < 15; ++i)
+        if (i < n) dst[i] = static_cast<char>(b[i]);
+}
+
 // The game's scalar leaves -> slab scalars, one per lane.
 __device__ __forceinline__ void load_scalars(const Params& P, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
@@ -325,23 +344,20 @@ __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t*
         if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(L.total_bytes));
         __syncwarp();
         if (lane < kSlabLeaves) bulk_load(slab + L.leaf_off[lane], global_row(P, lane, game), L.row_bytes[lane], bar);
-    } else if (lane == 0) {
-        uint32_t total = 0;
-        for (int k = 0; k < kSlabLeaves; ++k) total += split_row(global_row(P, k, game), L.row_bytes[k]).body;
-        mbar_arrive_expect_tx(bar, total);
-        for (int k = 0; k < kSlabLeaves; ++k) {
-            const char* src = global_row(P, k, game);
-            const Span sp = split_row(src, L.row_bytes[k]);
-            if (sp.body) bulk_load(slab_row(slab, L, k, src) + sp.head, src + sp.head, sp.body, bar);
+    } else {
+        // Lane k owns row k: the TMA bulk copy of its 16-byte-aligned body and
+        // its own unaligned head and tail bytes.
+        const char* src = lane < kSlabLeaves ? global_row(P, lane, game) : nullptr;
+        const Span sp = lane < kSlabLeaves ? split_row(src, L.row_bytes[lane]) : Span{0, 0, 0};
+        const uint32_t total = __reduce_add_sync(kFull, sp.body);
+        if (lane == 0) mbar_arrive_expect_tx(bar, total);
+        __syncwarp();
+        if (lane < kSlabLeaves) {
+            char* dst = slab_row(slab, L, lane, src);
+            if (sp.body) bulk_load(dst + sp.head, src + sp.head, sp.body, bar);
+            copy_edge_in(dst, src, sp.head);
+            copy_edge_in(dst + sp.head + sp.body, src + sp.head + sp.body, sp.tail);
         }
-    }
-    for (int k = 0; k < kSlabLeaves && !L.aligned; ++k) {
-        const char* src = global_row(P, k, game);
-        const Span sp = split_row(src, L.row_bytes[k]);
-        if (sp.head + sp.tail == 0) continue;
-        char* dst = slab_row(slab, L, k, src);
-        for (uint32_t i = lane; i < sp.head; i += 32) dst[i] = src[i];
-        for (uint32_t i = lane; i < sp.tail; i += 32) dst[sp.head + sp.body + i] = src[sp.head + sp.body + i];
     }
     load_scalars(P, slab, game, lane);
     const bool ok = wait_phase(bar, parity);
@@ -416,28 +432,21 @@ __device__ void store_state(const Params& P, char* slab, int64_t game, int lane)
             bulk_store(global_row(P, lane, game), slab + L.leaf_off[lane], L.row_bytes[lane]);
             bulk_commit();
         }
-    } else if (lane == 0) {
-        for (int k = 0; k < kSlabLeaves; ++k) {
-            char* dst = global_row(P, k, game);
-            const Span sp = split_row(dst, L.row_bytes[k]);
-            if (sp.body) bulk_store(dst + sp.head, slab_row(slab, L, k, dst) + sp.head, sp.body);
-        }
+    } else if (lane < kSlabLeaves) {  // lane k owns row k, as in stage_state
+        char* dst = global_row(P, lane, game);
+        const Span sp = split_row(dst, L.row_bytes[lane]);
+        const char* src = slab_row(slab, L, lane, dst);
+        if (sp.body) bulk_store(dst + sp.head, src + sp.head, sp.body);
         bulk_commit();
-    }
-    for (int k = 0; k < kSlabLeaves && !L.aligned; ++k) {
-        char* dst = global_row(P, k, game);
-        const Span sp = split_row(dst, L.row_bytes[k]);
-        if (sp.head + sp.tail == 0) continue;
-        const char* src = slab_row(slab, L, k, dst);
-        for (uint32_t i = lane; i < sp.head; i += 32) dst[i] = src[i];
-        for (uint32_t i = lane; i < sp.tail; i += 32) dst[sp.head + sp.body + i] = src[sp.head + sp.body + i];
+        copy_edge_out(dst, src, sp.head);
+        copy_edge_out(dst + sp.head + sp.body, src + sp.head + sp.body, sp.tail);
     }
     store_scalars(P, slab, game, lane);
 }
 
 // Waits until the slab rows read by this lane's bulk stores may be reused.
 __device__ __forceinline__ void finish_stores(const Params& P, int lane) {
-    if (P.layout.aligned ? lane < kSlabLeaves : lane == 0) bulk_wait_read_all();
+    if (lane < kSlabLeaves) bulk_wait_read_all();
 }
 
 // Order-preserving warp compaction of indices [0, n) satisfying `pred`.

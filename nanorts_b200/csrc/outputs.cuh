@@ -296,7 +296,7 @@ __device__ __forceinline__ void draw_row(uint32_t w0, uint32_t w1, uint32_t w2, 
 // each player occupies (the owner plane of board_view, model/board_view.py:44-69).
 template <int kW>
 __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, const Game& g, uint32_t* words, uint64_t* occ, bool rows,
-                                           int lane) {
+                                           int32_t entities, int lane) {
     auto word_of = [&](int32_t c) {
         const int32_t s = g.entity_at[c];
         const uint32_t wall_bit = ((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u;
@@ -320,17 +320,28 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
             }
         }
     } else if constexpr (kW == 64) {
-        for (int32_t row = 0; row < G.h; ++row) {
-            const int32_t c = row * 64 + lane;
-            const uint32_t lo = word_of(c), hi = word_of(c + 32);
-            words[c] = lo;
-            words[c + 32] = hi;
-            const unsigned lo0 = __ballot_sync(kFull, ((lo >> 28) & 3u) == 1u), hi0 = __ballot_sync(kFull, ((hi >> 28) & 3u) == 1u);
-            const unsigned lo1 = __ballot_sync(kFull, ((lo >> 28) & 3u) == 2u), hi1 = __ballot_sync(kFull, ((hi >> 28) & 3u) == 2u);
-            if (rows && lane == 0) {
-                occ[row] = static_cast<uint64_t>(lo0) | (static_cast<uint64_t>(hi0) << 32);
-                occ[G.h + row] = static_cast<uint64_t>(lo1) | (static_cast<uint64_t>(hi1) << 32);
-            }
+        // Wide boards hold few units per cell: the wall bits of every cell in
+        // 16-byte groups, then the occupant word of each cell entity_at names,
+        // found from the active slots (entity_at names exactly the active
+        // slots' cells, the State invariant of model/state.py:87-165).
+        if (rows)
+            for (int32_t r = lane; r < 2 * G.h; r += 32) occ[r] = 0ull;
+        for (int32_t q = lane; q < (G.cells >> 2); q += 32) {
+            const int32_t c = q << 2;
+            const uint32_t bits = static_cast<uint32_t>(H.terrain_rows[c >> 6] >> (c & 63)) & 0xfu;
+            reinterpret_cast<uint4*>(words)[q] = make_uint4(bits & 1u ? kWallBit : 0u, bits & 2u ? kWallBit : 0u,
+                                                            bits & 4u ? kWallBit : 0u, bits & 8u ? kWallBit : 0u);
+        }
+        __syncwarp();
+        for (int32_t s = lane; s < entities; s += 32) {
+            if (g.birth[s] == kAbsent) continue;
+            const int32_t c = g.cell[s];
+            if (c < 0 || c >= G.cells || g.entity_at[c] != s) continue;
+            const uint32_t w = occupant_word(g, s) | words[c];
+            words[c] = w;
+            const uint32_t code = (w >> 28) & 3u;
+            if (rows && (code == 1u || code == 2u))
+                atomicOr(reinterpret_cast<unsigned long long*>(&occ[(code - 1) * G.h + (c >> 6)]), 1ull << (c & 63));
         }
     } else {
         if (rows)
@@ -368,7 +379,7 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
     const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample || P.out.packed_masks[0] != nullptr ||
                             P.out.packed_masks[1] != nullptr;
     const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
-    cell_words(H, G, g, words, occ, want_masks, lane);
+    cell_words(H, G, g, words, occ, want_masks, P.entities, lane);
     if (want_masks) {
         // Types each player can afford (the balance rule of produce.py:25-35).
         uint32_t afford0 = 0u, afford1 = 0u;
