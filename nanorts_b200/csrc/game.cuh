@@ -449,6 +449,21 @@ __device__ __forceinline__ void finish_stores(const Params& P, int lane) {
     if (lane < kSlabLeaves) bulk_wait_read_all();
 }
 
+// The threads that write one game's outputs: its warp (tid = lane), or every
+// warp of a CTA that holds a single large game.
+struct Team {
+    int32_t tid, size;
+    __device__ __forceinline__ bool cta() const { return size > 32; }
+    __device__ __forceinline__ int32_t lane() const { return tid & 31; }
+    __device__ __forceinline__ int32_t warp() const { return tid >> 5; }
+    __device__ __forceinline__ void sync() const {
+        if (cta()) __syncthreads();
+        else __syncwarp();
+    }
+};
+
+__device__ __forceinline__ Team warp_team(int lane) { return Team{lane, 32}; }
+
 // Order-preserving warp compaction of indices [0, n) satisfying `pred`.
 template <typename Pred>
 __device__ __forceinline__ int32_t warp_compact(int32_t n, int lane, int16_t* out, Pred pred) {

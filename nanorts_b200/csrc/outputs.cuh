@@ -32,10 +32,10 @@ __device__ __forceinline__ uint32_t occupant_word(const Game& g, int32_t s) {
 
 // Disks of sight of each player's units (observations/visibility.py:70-77).
 template <int kW>
-__device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, uint64_t* vis, int lane) {
-    for (int32_t r = lane; r < 2 * G.h; r += 32) vis[r] = 0ull;
-    __syncwarp();
-    for (int32_t p = lane; p < P.owned; p += 32) {
+__device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, uint64_t* vis, const Team& T) {
+    for (int32_t r = T.tid; r < 2 * G.h; r += T.size) vis[r] = 0ull;
+    T.sync();
+    for (int32_t p = T.tid; p < P.owned; p += T.size) {
         const int32_t s = P.neutral + p;
         if (!g.active(s)) continue;
         const int32_t player = p >= P.capacity;
@@ -53,7 +53,7 @@ __device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>&
             if (dy > 0 && uy + dy < G.h) atomicOr(reinterpret_cast<unsigned long long*>(&vis[player * G.h + uy + dy]), bits);
         }
     }
-    __syncwarp();
+    T.sync();
 }
 
 // Neighbour facts from occupant words (board.py:23-61 over board_view).
@@ -150,7 +150,7 @@ __device__ __forceinline__ uint32_t chunk_bits(const uint32_t* rows, int32_t r, 
 // One player's legality rows [C, width] of this game, as 0/1 bytes: full
 // 16-byte chunks by vector stores (row and column advanced incrementally),
 // the bytes before the first and after the last full chunk one by one.
-__device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game, uint8_t* out, int lane) {
+__device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game, uint8_t* out, const Team& T) {
     const int32_t width = P.mask_width;
     const int32_t span = P.capacity * width;
     uint8_t* base = out + game * static_cast<int64_t>(span);
@@ -158,17 +158,17 @@ __device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game,
     const int32_t full = (span - head) >> 4;
     const int32_t tail_start = head + 16 * full;
     const int32_t loose = head + (span - tail_start);
-    for (int32_t k = lane; k < loose; k += 32) {
+    for (int32_t k = T.tid; k < loose; k += T.size) {
         const int32_t o = k < head ? k : tail_start + (k - head);
         const int32_t r = o / width, c = o - r * width;
         base[o] = static_cast<uint8_t>(row_bits(rows, r, c) & 1u);
     }
     if (full == 0) return;
-    const int32_t step = 16 * 32;
+    const int32_t step = 16 * T.size;
     const int32_t step_rows = step / width, step_cols = step - step_rows * width;
-    const int32_t o = head + 16 * lane;
+    const int32_t o = head + 16 * T.tid;
     int32_t r = o / width, c = o - r * width;
-    for (int32_t k = lane; k < full; k += 32) {
+    for (int32_t k = T.tid; k < full; k += T.size) {
         const uint32_t bits = chunk_bits(rows, r, c, width);
         uint4 v;
         v.x = spread4(bits & 0xfu);
@@ -187,13 +187,13 @@ __device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game,
 
 // One player's legality rows in the packed form (adapters/factors.py:89-103):
 // word 0 = the first 6+16+T bits, words 1-2 = the attack window's bits.
-__device__ void write_packed(const Params& P, const uint32_t* rows, int64_t game, uint32_t* out, int lane) {
+__device__ void write_packed(const Params& P, const uint32_t* rows, int64_t game, uint32_t* out, const Team& T) {
     const int32_t head = P.mask_width - P.offsets;
     const uint32_t head_mask = (1u << head) - 1u;
     const uint32_t hi_mask = P.offsets > 32 ? ((P.offsets >= 64) ? ~0u : ((1u << (P.offsets - 32)) - 1u)) : 0u;
     const uint32_t lo_mask = P.offsets >= 32 ? ~0u : ((1u << P.offsets) - 1u);
     uint32_t* base = out + game * static_cast<int64_t>(P.capacity) * 3;
-    for (int32_t r = lane; r < P.capacity; r += 32) {
+    for (int32_t r = T.tid; r < P.capacity; r += T.size) {
         const uint32_t w0 = rows[3 * r], w1 = rows[3 * r + 1], w2 = rows[3 * r + 2];
         base[3 * r] = w0 & head_mask;
         base[3 * r + 1] = __funnelshift_r(w0, w1, head) & lo_mask;
@@ -213,7 +213,7 @@ __device__ __forceinline__ void features(uint32_t w, int player, bool shown, uin
 
 template <int kW>
 __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game& g, const uint32_t* words, const uint64_t* vis, int player,
-                                  int64_t game, uint8_t* maps, int32_t* scalars, int lane) {
+                                  int64_t game, uint8_t* maps, int32_t* scalars, const Team& T) {
     if (maps != nullptr) {
         uint8_t* base = maps + game * static_cast<int64_t>(G.cells) * kFeatures;
         auto cell_features = [&](int32_t c, uint32_t& lo, uint32_t& hi) {
@@ -227,7 +227,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
         };
         if ((G.cells & 7) == 0 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
             // 8 cells = 48 bytes = three 16-byte stores; two cells fill three words.
-            for (int32_t c0 = lane * 8; c0 < G.cells; c0 += 32 * 8) {
+            for (int32_t c0 = T.tid * 8; c0 < G.cells; c0 += T.size * 8) {
                 uint32_t w[12];
 #pragma unroll
                 for (int pair = 0; pair < 4; ++pair) {
@@ -244,7 +244,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
                 dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
             }
         } else {
-            for (int32_t c = lane; c < G.cells; c += 32) {
+            for (int32_t c = T.tid; c < G.cells; c += T.size) {
                 uint32_t lo, hi;
                 cell_features(c, lo, hi);
                 for (int b = 0; b < 4; ++b) base[c * kFeatures + b] = static_cast<uint8_t>(lo >> (8 * b));
@@ -253,7 +253,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
             }
         }
     }
-    if (scalars != nullptr && lane == 0) {  // symbolic.py:171-180
+    if (scalars != nullptr && T.tid == 0) {  // symbolic.py:171-180
         *reinterpret_cast<int4*>(scalars + game * kScalars) =
             make_int4(g.s[kSRes0 + player], g.s[kSRes0 + 1 - player], g.s[kSTime], g.s[kSAlt]);
     }
@@ -296,7 +296,8 @@ __device__ __forceinline__ void draw_row(uint32_t w0, uint32_t w1, uint32_t w2, 
 // each player occupies (the owner plane of board_view, model/board_view.py:44-69).
 template <int kW>
 __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, const Game& g, uint32_t* words, uint64_t* occ, bool rows,
-                                           int32_t entities, int lane) {
+                                           int32_t entities, const Team& T) {
+    const int32_t lane = T.lane();
     auto word_of = [&](int32_t c) {
         const int32_t s = g.entity_at[c];
         const uint32_t wall_bit = ((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u;
@@ -305,7 +306,7 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
     if constexpr (kW > 0 && kW <= 32) {
         constexpr int kRowsPerChunk = 32 / kW;
         constexpr uint32_t kMask = kW == 32 ? ~0u : ((1u << kW) - 1u);
-        for (int32_t base = 0; base < G.cells; base += 32) {
+        for (int32_t base = 32 * T.warp(); base < G.cells; base += T.size) {
             const int32_t c = base + lane;
             const uint32_t w = c < G.cells ? word_of(c) : 0u;
             if (c < G.cells) words[c] = w;
@@ -325,15 +326,15 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
         // found from the active slots (entity_at names exactly the active
         // slots' cells, the State invariant of model/state.py:87-165).
         if (rows)
-            for (int32_t r = lane; r < 2 * G.h; r += 32) occ[r] = 0ull;
-        for (int32_t q = lane; q < (G.cells >> 2); q += 32) {
+            for (int32_t r = T.tid; r < 2 * G.h; r += T.size) occ[r] = 0ull;
+        for (int32_t q = T.tid; q < (G.cells >> 2); q += T.size) {
             const int32_t c = q << 2;
             const uint32_t bits = static_cast<uint32_t>(H.terrain_rows[c >> 6] >> (c & 63)) & 0xfu;
             reinterpret_cast<uint4*>(words)[q] = make_uint4(bits & 1u ? kWallBit : 0u, bits & 2u ? kWallBit : 0u,
                                                             bits & 4u ? kWallBit : 0u, bits & 8u ? kWallBit : 0u);
         }
-        __syncwarp();
-        for (int32_t s = lane; s < entities; s += 32) {
+        T.sync();
+        for (int32_t s = T.tid; s < entities; s += T.size) {
             if (g.birth[s] == kAbsent) continue;
             const int32_t c = g.cell[s];
             if (c < 0 || c >= G.cells || g.entity_at[c] != s) continue;
@@ -345,32 +346,32 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
         }
     } else {
         if (rows)
-            for (int32_t r = lane; r < 2 * G.h; r += 32) occ[r] = 0ull;
-        __syncwarp();
-        for (int32_t c = lane; c < G.cells; c += 32) {
+            for (int32_t r = T.tid; r < 2 * G.h; r += T.size) occ[r] = 0ull;
+        T.sync();
+        for (int32_t c = T.tid; c < G.cells; c += T.size) {
             const uint32_t w = word_of(c);
             words[c] = w;
             const uint32_t owner = (w >> 28) & 3u;
             if (rows && owner != 0u) atomicOr(reinterpret_cast<unsigned long long*>(&occ[(owner - 1) * G.h + G.y(c)]), 1ull << G.x(c));
         }
     }
-    __syncwarp();
+    T.sync();
 }
 
 // Zero int32 [count] at dst (4-byte aligned) with 16-byte stores where aligned.
-__device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, int lane) {
+__device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, const Team& T) {
     const int32_t head = min(count, static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2));
     const int32_t quads = (count - head) >> 2;
     const int32_t tail = head + 4 * quads;
-    if (lane < head) dst[lane] = 0;
+    if (T.tid < head) dst[T.tid] = 0;
     uint4* body = reinterpret_cast<uint4*>(dst + head);
-    for (int32_t k = lane; k < quads; k += 32) body[k] = make_uint4(0u, 0u, 0u, 0u);
-    if (lane < count - tail) dst[tail + lane] = 0;
+    for (int32_t k = T.tid; k < quads; k += T.size) body[k] = make_uint4(0u, 0u, 0u, 0u);
+    if (T.tid < count - tail) dst[tail + T.tid] = 0;
 }
 
 template <int kW>
 __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
-                              uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2], bool sample, int lane) {
+                              uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2], bool sample, const Team& T) {
     const Layout& L = P.layout;
     uint32_t* words = reinterpret_cast<uint32_t*>(slab + L.word_off);
     uint64_t* occ = reinterpret_cast<uint64_t*>(slab + L.rows_off);
@@ -379,7 +380,7 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
     const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample || P.out.packed_masks[0] != nullptr ||
                             P.out.packed_masks[1] != nullptr;
     const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
-    cell_words(H, G, g, words, occ, want_masks, P.entities, lane);
+    cell_words(H, G, g, words, occ, want_masks, P.entities, T);
     if (want_masks) {
         // Types each player can afford (the balance rule of produce.py:25-35).
         uint32_t afford0 = 0u, afford1 = 0u;
@@ -390,27 +391,32 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
         }
         if (sample) {  // every row draws 0 unless it holds an available unit (written below)
             for (int player = 0; player < kPlayers; ++player)
-                zero_words(P.sampled[player] + game * P.capacity * kActionColumns, P.capacity * kActionColumns, lane);
+                zero_words(P.sampled[player] + game * P.capacity * kActionColumns, P.capacity * kActionColumns, T);
         }
         // Rows of slots without an available unit hold only KIND_NONE; the
-        // available ones are listed and computed densely.
+        // available ones are listed (by the first warp) and computed densely.
         int16_t* avail = reinterpret_cast<int16_t*>(slab + L.list_off);
         int32_t A = 0;
-        for (int32_t base = 0; base < P.owned; base += 32) {
-            const int32_t p = base + lane;
-            const bool in = p < P.owned;
-            const bool available = in && g.birth[P.neutral + p] != kAbsent && g.pending_kind[P.neutral + p] == kAbsent;
-            if (in && !available) {
-                rows[3 * p] = 1u;
-                rows[3 * p + 1] = 0u;
-                rows[3 * p + 2] = 0u;
+        if (T.warp() == 0) {
+            const int lane = T.lane();
+            for (int32_t base = 0; base < P.owned; base += 32) {
+                const int32_t p = base + lane;
+                const bool in = p < P.owned;
+                const bool available = in && g.birth[P.neutral + p] != kAbsent && g.pending_kind[P.neutral + p] == kAbsent;
+                if (in && !available) {
+                    rows[3 * p] = 1u;
+                    rows[3 * p + 1] = 0u;
+                    rows[3 * p + 2] = 0u;
+                }
+                const unsigned m = __ballot_sync(kFull, available);
+                if (available) avail[A + __popc(m & lanes_below(lane))] = static_cast<int16_t>(p);
+                A += __popc(m);
             }
-            const unsigned m = __ballot_sync(kFull, available);
-            if (available) avail[A + __popc(m & lanes_below(lane))] = static_cast<int16_t>(p);
-            A += __popc(m);
+            if (T.cta() && lane == 0) rows[3 * P.owned] = static_cast<uint32_t>(A);
         }
-        __syncwarp();
-        for (int32_t i = lane; i < A; i += 32) {
+        T.sync();
+        if (T.cta()) A = static_cast<int32_t>(rows[3 * P.owned]);
+        for (int32_t i = T.tid; i < A; i += T.size) {
             const int32_t p = avail[i];
             uint32_t w0, w1, w2;
             legality_row(P, H, G, g, words, occ, afford0, afford1, p, w0, w1, w2);
@@ -427,19 +433,19 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
                 for (int f = 0; f < kActionColumns; ++f) dst[f] = a[f];
             }
         }
-        __syncwarp();
+        T.sync();
         for (int player = 0; player < kPlayers; ++player) {
-            if (masks[player] != nullptr) write_masks(P, rows + player * P.capacity * 3, game, masks[player], lane);
+            if (masks[player] != nullptr) write_masks(P, rows + player * P.capacity * 3, game, masks[player], T);
             if (P.out.packed_masks[player] != nullptr)
-                write_packed(P, rows + player * P.capacity * 3, game, P.out.packed_masks[player], lane);
+                write_packed(P, rows + player * P.capacity * 3, game, P.out.packed_masks[player], T);
         }
     }
     if (want_obs) {
-        if (P.partial) visibility_rows(P, H, G, g, vis, lane);
+        if (P.partial) visibility_rows(P, H, G, g, vis, T);
         for (int player = 0; player < kPlayers; ++player)
-            write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], lane);
+            write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], T);
     }
-    __syncwarp();
+    T.sync();
 }
 
 }  // namespace nrts

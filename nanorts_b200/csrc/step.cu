@@ -79,7 +79,7 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
     }
     if (P.out.final_feature_maps[0] || P.out.final_feature_maps[1] || P.out.final_scalars[0] || P.out.final_scalars[1]) {
         uint8_t* const no_masks[2] = {nullptr, nullptr};
-        write_outputs(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false, lane);
+        write_outputs(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false, warp_team(lane));
     }
     if (done) {  // lifecycle.advance: the next episode starts from the reset State
         const int32_t episode = g.s[kSEpisode];
@@ -96,10 +96,11 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
     return done;
 }
 
-// One game through the launch's mode; false when a bounded wait gave up.
+// A game's State through the launch's mode, up to issuing its stores; false
+// when a bounded wait gave up.
 template <int kW>
-__device__ __forceinline__ bool run_game(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
-                                         uint32_t parity, int64_t game, int lane) {
+__device__ __forceinline__ bool game_core(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
+                                          uint32_t parity, int64_t game, int lane) {
     Game g = game_view(P, slab, game);
     if (P.mode == kModeReset) {
         load_reset(P, slab, game, lane);
@@ -118,7 +119,16 @@ __device__ __forceinline__ bool run_game(const Params& P, const Header& H, const
         finish_core_step(P, H, G, g, slab, game, lane);
     }
     if (P.mode != kModeOutputs) store_state(P, slab, game, lane);
-    write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, lane);
+    return true;
+}
+
+// One game through the launch's mode on its warp; false when a bounded wait gave up.
+template <int kW>
+__device__ __forceinline__ bool run_game(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
+                                         uint32_t parity, int64_t game, int lane) {
+    if (!game_core(P, H, G, slab, bar, parity, game, lane)) return false;
+    const Game g = game_view(P, slab, game);
+    write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, warp_team(lane));
     if (P.mode != kModeOutputs) finish_stores(P, lane);
     __syncwarp();
     return true;
@@ -154,6 +164,46 @@ __device__ __forceinline__ void step_block(const Params& P, int64_t block, int64
 template <int kW>
 __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Params P) {
     step_block<kW>(P, blockIdx.x, gridDim.x);
+}
+
+// Wide boards (a slab too large for more than a few games per SM): one game
+// per CTA of kTeamWarps warps.  Warp 0 runs the game's State through the
+// launch's mode; then every warp writes its outputs.
+constexpr int kTeamWarps = 4;
+constexpr int32_t kWideSlabBytes = 24 * 1024;  // above this a game gets a CTA of its own
+
+template <int kW>
+__global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __grid_constant__ Params P) {
+    extern __shared__ __align__(128) char smem[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const Team T{static_cast<int32_t>(threadIdx.x), static_cast<int32_t>(blockDim.x)};
+    const Layout& L = P.layout;
+    const Header H = setup_header(P, smem);
+    const Geo<kW> G{P.width, P.height, P.cells};
+    char* slab = smem + L.header_bytes;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(slab + L.bar_off);
+    volatile int32_t* ok = reinterpret_cast<int32_t*>(slab + L.bar_off + 8);  // beside the mbarrier
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    uint32_t parity = 0;
+    for (int64_t g0 = blockIdx.x; g0 < P.lanes; g0 += gridDim.x) {
+        const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
+        if (warp == 0) {
+            const bool done = game_core(P, H, G, slab, bar, parity, game, lane);
+            if (lane == 0) *ok = done;
+        }
+        __syncthreads();
+        if (!*ok) break;
+        const Game g = game_view(P, slab, game);
+        write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, T);
+        if (warp == 0 && P.mode != kModeOutputs) finish_stores(P, lane);
+        __syncthreads();
+        if (P.mode != kModeReset) parity ^= 1u;
+    }
 }
 
 // Several groups of games in one launch: the CTAs of group k are the blocks
@@ -217,7 +267,7 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
     const NrtsOutputs& o = P.out;
     if (o.masks[0] || o.masks[1] || o.packed_masks[0] || o.packed_masks[1] || o.feature_maps[0] || o.feature_maps[1] ||
         o.scalars[0] || o.scalars[1] || P.sampled[0])
-        write_outputs(P, H, G, g, slab, game, o.masks, o.feature_maps, o.scalars, P.sampled[0] != nullptr, lane);
+        write_outputs(P, H, G, g, slab, game, o.masks, o.feature_maps, o.scalars, P.sampled[0] != nullptr, warp_team(lane));
     finish_bot_stores();
     __syncwarp();
     return true;
@@ -405,6 +455,16 @@ struct DeviceInfo {
 
 DeviceInfo g_devices[64];
 
+const void* pick_wide_kernel(int width) {
+    switch (width) {
+        case 8: return reinterpret_cast<const void*>(step_kernel_wide<8>);
+        case 16: return reinterpret_cast<const void*>(step_kernel_wide<16>);
+        case 32: return reinterpret_cast<const void*>(step_kernel_wide<32>);
+        case 64: return reinterpret_cast<const void*>(step_kernel_wide<64>);
+        default: return reinterpret_cast<const void*>(step_kernel_wide<0>);
+    }
+}
+
 const void* pick_groups_kernel(int width) {
     switch (width) {
         case 8: return reinterpret_cast<const void*>(groups_kernel<8>);
@@ -448,6 +508,8 @@ int prepare_device(int& device, DeviceInfo*& info) {
             }
             if (cudaFuncSetAttribute(pick_groups_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(groups kernel) failed");
+            if (cudaFuncSetAttribute(pick_wide_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(wide kernel) failed");
         }
         info->ready = true;
     }
@@ -532,8 +594,25 @@ int launch_step(Params& P, void* stream) {
     if (P.lanes == 0) return NRTS_OK;
     const Layout& L = P.layout;
     if (L.header_bytes + L.slab_bytes > info->smem_optin) return fail(NRTS_E_ARGUMENT, "one game does not fit in shared memory");
+    const bool bots = P.mode == kModeDuel || P.mode == kModeBotAct;
+    if (!bots && L.slab_bytes > kWideSlabBytes) {
+        // Few games fit per SM: give each one a CTA of kTeamWarps warps.
+        const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
+        const unsigned blocks = static_cast<unsigned>(P.lanes);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        switch (P.width) {
+            case 8: step_kernel_wide<8><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+            case 16: step_kernel_wide<16><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+            case 32: step_kernel_wide<32><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+            case 64: step_kernel_wide<64><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+            default: step_kernel_wide<0><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+        }
+        const cudaError_t err = cudaGetLastError();
+        if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("wide kernel launch: ") + cudaGetErrorString(err));
+        return NRTS_OK;
+    }
     // Warps per CTA with the most games resident per SM (registers and shared memory).
-    const void* kernel = pick_kernel(P.width, P.mode == kModeDuel || P.mode == kModeBotAct);
+    const void* kernel = pick_kernel(P.width, bots);
     int best_warps = 1, best_resident = 0;
     for (int warps = 1; warps <= 8; ++warps) {
         const size_t smem = L.header_bytes + static_cast<size_t>(warps) * L.slab_bytes;
@@ -867,7 +946,8 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
         const void* kernels[] = {pick_kernel(8), pick_kernel(16), pick_kernel(32), pick_kernel(64), pick_kernel(7),
                                  pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
                                  pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
-                                 pick_groups_kernel(64), pick_groups_kernel(7),
+                                 pick_groups_kernel(64), pick_groups_kernel(7), pick_wide_kernel(8), pick_wide_kernel(16),
+                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
                                  reinterpret_cast<const void*>(probe_kernel)};
         for (const void* k : kernels) {

@@ -40,6 +40,9 @@ CONFIGS = {
                                            ConflictStrategy.CANCEL_ALTERNATING, partial=True),
     "c5_64x64_random": Config("c5_64x64_random", "GardenOfWar64x64", O, ConflictStrategy.CANCEL_RANDOM,
                               capacity_profile=False),
+    # A wide board with partial observability: the visibility rows of the one-game-per-CTA kernel.
+    "c5_64x64_alternating_partial": Config("c5_64x64_alternating_partial", "GardenOfWar64x64", F,
+                                           ConflictStrategy.CANCEL_ALTERNATING, partial=True, capacity_profile=False),
 }
 
 
