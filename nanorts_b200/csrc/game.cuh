@@ -50,20 +50,21 @@ struct Layout {
     int32_t leaf_off[kSlabLeaves];
     int32_t row_bytes[kSlabLeaves];
     int32_t scal_off;
-    int32_t list_off;    // int16 [2C]: requests, then members
+    int32_t list_off;    // int16 [2C]: requests, then members, then the available units
     int32_t order_off;   // int16 [2C]: sorted requests, then sorted members
+    // Admission scratch.
+    int32_t serial_off;  // int16 [2C] ranks of the contested requests
     int32_t scan_off;    // int16 [E]:  claim holders scanned by contested requests
     int32_t conf_off;    // int16 [E]:  conflicting holders
-    int32_t free_off;    // uint32 [2 * ceil(C/32)]: free slots of each player block
-    // Admission scratch.
     int32_t key_off;     // uint32 [2C] sort keys
     int32_t info_off;    // ReqInfo [2C]
     int32_t rank_off;    // int16 [2C] admission rank of each owned slot's request (-1 none)
-    int32_t serial_off;  // int16 [2C] ranks of the contested requests
     int32_t count_off;   // uint8 [cells rounded to 4] claims per cell, 2 x uint32 produce claims, 2 x 5 int32 reward-component counts
-    // Completion scratch (aliases admission scratch).
+    // Completion and outcome scratch (aliases admission scratch).
+    int32_t free_off;    // uint32 [2 * ceil(C/32)]: free slots of each player block
+    int32_t member_key_off;  // uint32 [2C] pending-order keys of the completing members
     int32_t ret_off;     // Retained [2C]
-    // Epilogue scratch (aliases both).
+    // Epilogue scratch (aliases both, and `order` when no bots run).
     int32_t word_off;    // uint32 [cells] occupant words
     int32_t rows_off;    // uint64 [4H] occupancy (2) and visibility (2) rows
     int32_t mask_off;    // uint32 [2C * 3 + 2] legality row words

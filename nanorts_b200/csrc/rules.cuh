@@ -107,9 +107,11 @@ __device__ bool can_execute(const Params& P, const Header& H, const Geo<kW>& G, 
 
 // One admission request, decided before the ordered loop: legality, blocking,
 // durations and the claimed cell read only fields admission never changes.
+// `duration` is the requested duration (admission.py:247-253) of a kind other
+// than NONE, and the none duration of a request whose kind, after the
+// legality and blocking rules, is NONE: only one of the two is ever read.
 struct ReqInfo {
-    int32_t requested;  // requested duration (admission.py:247-253)
-    int32_t none;       // none duration after the legality and blocking rules
+    int32_t duration;
     int16_t target;     // attack target cell or -1
     int16_t pos;        // reserved position (claimed cell when kind claims)
     int8_t kind;        // kind after the legality and blocking rules
@@ -117,7 +119,7 @@ struct ReqInfo {
     int8_t ptype;       // canonical produced type
     uint8_t serial;     // needs the ordered conflict loop
 };
-static_assert(sizeof(ReqInfo) == 16, "request info");
+static_assert(sizeof(ReqInfo) == 12, "request info");
 
 struct Retained {
     int32_t birth;
@@ -206,7 +208,9 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
         const int32_t slot = N + list[i];
         const ReqInfo q = info[i];
         const int32_t ord = static_cast<int32_t>(keys[i]);
-        int32_t kind = q.kind, none = q.none;
+        // Only a claiming or paying kind (never NONE) meets conflicts below,
+        // so q.duration is its requested duration wherever `before` reads it.
+        int32_t kind = q.kind, none = q.duration;
         const bool rclaims = claims_kind(kind);
         const int32_t rcost = kind_cost(P, H, kind, q.ptype);
         const int32_t rplayer = clampi(g.owner[slot], 0, kPlayers - 1);
@@ -279,7 +283,7 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
                         cancels_pending = !cancels_request;
                     }
                     if (cancels_pending) {  // _settle_durations, _cancel_pending
-                        const int32_t before = cross_seen ? -1 : min(q.requested, cap);
+                        const int32_t before = cross_seen ? -1 : min(q.duration, cap);
                         const int32_t settled = min(dur, before);
                         g.pending_kind[e] = kKindNone;
                         g.pending_direction[e] = kAbsent;
@@ -294,10 +298,10 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
                 if (P.strategy == 2) g.s[kSAlt] = alt + same_before;
                 if (cross_seen || cap != kNoCap) {
                     kind = kKindNone;
-                    none = cross_seen ? -1 : min(q.requested, cap);
+                    none = cross_seen ? -1 : min(q.duration, cap);
                 }
             }
-            assign_pending(g, slot, kind, none, q.requested, q.dir, q.target, q.ptype, time, ord);
+            assign_pending(g, slot, kind, none, q.duration, q.dir, q.target, q.ptype, time, ord);
             if (claims_kind(kind)) scan[holders] = static_cast<int16_t>(slot);
         }
         __syncwarp();
@@ -406,8 +410,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                 if (kind == kKindProduce) atomicAdd(&produce_claims[player], 1u);
                 if (counting) count_event(P, g, events + player * kEventCounts, player, kind, cptype, target);
                 ReqInfo r;
-                r.requested = requested;
-                r.none = none;
+                r.duration = kind == kKindNone ? none : requested;
                 r.target = static_cast<int16_t>(target);
                 r.pos = static_cast<int16_t>(pos);
                 r.kind = narrow8(kind);
@@ -501,7 +504,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
             if (serial) {
                 info[i].serial = 1;
             } else {
-                assign_pending(g, slot, q.kind, q.none, q.requested, q.dir, q.target, q.ptype, time, ord);
+                assign_pending(g, slot, q.kind, q.duration, q.duration, q.dir, q.target, q.ptype, time, ord);
             }
         }
         appended += __popc(m);
@@ -533,7 +536,7 @@ __device__ void complete(const Params& P, const Header& H, const Geo<kW>& G, Gam
     const int32_t N = P.neutral, E = P.entities, C = P.capacity;
     int16_t* list = reinterpret_cast<int16_t*>(slab + L.list_off);
     int16_t* order = reinterpret_cast<int16_t*>(slab + L.order_off);
-    uint32_t* keys = reinterpret_cast<uint32_t*>(slab + L.key_off);
+    uint32_t* keys = reinterpret_cast<uint32_t*>(slab + L.member_key_off);
     Retained* ret = reinterpret_cast<Retained*>(slab + L.ret_off);
     uint32_t* free_words = reinterpret_cast<uint32_t*>(slab + L.free_off);
     const int32_t time = static_cast<int32_t>(static_cast<uint32_t>(g.s[kSTime]) + 1u);  // pending.select

@@ -166,6 +166,18 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Pa
     step_block<kW>(P, blockIdx.x, gridDim.x);
 }
 
+// One CTA per SM holding as many games (one per warp) as its shared memory
+// takes, up to kBigWarps: no per-CTA reserve or header copy is paid more than
+// once per SM, which fits more games per SM than CTAs of at most 8 warps.
+// The grid is persistent (one CTA per SM; each warp steps every
+// (SMs * warps)-th game).
+constexpr int kBigWarps = 28;
+
+template <int kW>
+__global__ void __launch_bounds__(32 * kBigWarps, 1) step_kernel_big(const __grid_constant__ Params P) {
+    step_block<kW>(P, blockIdx.x, gridDim.x);
+}
+
 // Wide boards (a slab too large for more than a few games per SM): one game
 // per CTA of kTeamWarps warps.  Warp 0 runs the game's State through the
 // launch's mode; then every warp writes its outputs.
@@ -405,31 +417,30 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     off += round16(owned * 2);
     L.order_off = off;
     off += round16(owned * 2);
-    L.serial_off = off;
-    off += round16(owned * 2);
-    L.scan_off = off;
-    off += round16(E * 2);
-    L.conf_off = off;
-    off += round16(E * 2);
-    L.free_off = off;
-    off += round16(2 * free_words * 4);
     if (bots) {
         L.carry_off = off;
         off += 2 * carry_bytes(x->capacity);
         L.cmd_off = off;
         off += cmd_layout(owned, 0).bytes;
     }
-    // Scratch shared by the bots, admission, completion and the epilogue, in turn.
+    // Scratch shared in turn by the bots, admission, completion (with the
+    // outcome that reads its free-slot bitmaps) and the epilogue.  The
+    // epilogue keeps only `list` (its available units) and starts at `order`.
     const int32_t U = off;
-    L.key_off = U;
-    L.info_off = U + round16(owned * 4);
-    L.rank_off = L.info_off + round16(owned * 16);
+    L.serial_off = U;
+    L.scan_off = L.serial_off + round16(owned * 2);
+    L.conf_off = L.scan_off + round16(E * 2);
+    L.key_off = L.conf_off + round16(E * 2);
+    L.info_off = L.key_off + round16(owned * 4);
+    L.rank_off = L.info_off + round16(owned * 12);
     L.count_off = L.rank_off + round16(owned * 2);
     const int32_t end_admission = L.count_off + round16(((cells + 3) / 4) * 4 + 8 + 2 * 5 * 4);
-    L.ret_off = U + round16(owned * 4);
+    L.free_off = U;
+    L.member_key_off = L.free_off + round16(2 * free_words * 4);
+    L.ret_off = L.member_key_off + round16(owned * 4);
     const int32_t end_completion = L.ret_off + round16(owned * 20);
-    L.word_off = U;
-    L.rows_off = U + round16(cells * 4);
+    L.word_off = bots ? U : L.order_off;
+    L.rows_off = L.word_off + round16(cells * 4);
     L.mask_off = L.rows_off + round16(4 * x->height * 8);
     const int32_t end_epilogue = L.mask_off + round16((owned * 3 + 2) * 4);
     off = std::max(end_admission, std::max(end_completion, end_epilogue));
@@ -462,6 +473,16 @@ const void* pick_wide_kernel(int width) {
         case 32: return reinterpret_cast<const void*>(step_kernel_wide<32>);
         case 64: return reinterpret_cast<const void*>(step_kernel_wide<64>);
         default: return reinterpret_cast<const void*>(step_kernel_wide<0>);
+    }
+}
+
+const void* pick_big_kernel(int width) {
+    switch (width) {
+        case 8: return reinterpret_cast<const void*>(step_kernel_big<8>);
+        case 16: return reinterpret_cast<const void*>(step_kernel_big<16>);
+        case 32: return reinterpret_cast<const void*>(step_kernel_big<32>);
+        case 64: return reinterpret_cast<const void*>(step_kernel_big<64>);
+        default: return reinterpret_cast<const void*>(step_kernel_big<0>);
     }
 }
 
@@ -510,6 +531,8 @@ int prepare_device(int& device, DeviceInfo*& info) {
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(groups kernel) failed");
             if (cudaFuncSetAttribute(pick_wide_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(wide kernel) failed");
+            if (cudaFuncSetAttribute(pick_big_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(big kernel) failed");
         }
         info->ready = true;
     }
@@ -622,6 +645,29 @@ int launch_step(Params& P, void* stream) {
         if (blocks * warps >= best_resident) {
             best_resident = blocks * warps;
             best_warps = warps;
+        }
+    }
+    if (!bots) {
+        // One CTA per SM when that holds more games and the batch fills it.
+        const int64_t room = (static_cast<int64_t>(info->smem_optin) - L.header_bytes) / L.slab_bytes;
+        const int big = static_cast<int>(std::min<int64_t>(kBigWarps, room));
+        int blocks = 0;
+        const size_t smem = L.header_bytes + static_cast<size_t>(big) * L.slab_bytes;
+        if (big > best_resident && P.lanes >= static_cast<int64_t>(info->sms) * big &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, pick_big_kernel(P.width), big * 32, smem) == cudaSuccess &&
+            blocks >= 1) {
+            const unsigned grid = static_cast<unsigned>(info->sms);
+            cudaStream_t s = static_cast<cudaStream_t>(stream);
+            switch (P.width) {
+                case 8: step_kernel_big<8><<<grid, big * 32, smem, s>>>(P); break;
+                case 16: step_kernel_big<16><<<grid, big * 32, smem, s>>>(P); break;
+                case 32: step_kernel_big<32><<<grid, big * 32, smem, s>>>(P); break;
+                case 64: step_kernel_big<64><<<grid, big * 32, smem, s>>>(P); break;
+                default: step_kernel_big<0><<<grid, big * 32, smem, s>>>(P); break;
+            }
+            const cudaError_t err = cudaGetLastError();
+            if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("big kernel launch: ") + cudaGetErrorString(err));
+            return NRTS_OK;
         }
     }
     int warps = best_warps;
@@ -947,7 +993,8 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                                  pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
                                  pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
                                  pick_groups_kernel(64), pick_groups_kernel(7), pick_wide_kernel(8), pick_wide_kernel(16),
-                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7),
+                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_big_kernel(8),
+                                 pick_big_kernel(16), pick_big_kernel(32), pick_big_kernel(64), pick_big_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
                                  reinterpret_cast<const void*>(probe_kernel)};
         for (const void* k : kernels) {

@@ -131,6 +131,15 @@ def test_parity_contested_moves(config_name):
         assert stats["alt"].max() > 0  # CANCEL_ALTERNATING counted conflicts
 
 
+@pytest.mark.parametrize("config_name,lanes", [("c2_16x16_random", 4096), ("c1_8x8_both", 4400),
+                                               ("c3_16x16_alternating_partial", 3600)])
+def test_parity_full_batches(config_name, lanes):
+    """Batches large enough to fill every SM: the launch that holds one CTA of
+    up to 28 games per SM (a persistent grid)."""
+    stats = run_parity(config_name, lanes=lanes, steps=60, seed=17, max_cycles=40, move_bias=0.3)
+    assert stats["episodes"] > 0
+
+
 @pytest.mark.parametrize("config_name", ["c5_64x64_random", "c5_64x64_alternating_partial"])
 def test_parity_garden_of_war(config_name):
     """64 x 64 boards: one game per CTA, its outputs written by every warp."""
