@@ -112,9 +112,21 @@ def load_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-def load_traffic(workload: str = "random") -> float | None:
+# The kernel each configuration's step launches on a B200 (148 SMs) and the
+# committed ncu summary holding its DRAM bytes per env-step.
+KERNELS = {
+    1: ("nrts::step_kernel<8>", None),
+    2: ("nrts::step_kernel_big<16>", "step_kernel_16x16_traffic.txt"),
+    3: ("nrts::step_kernel_big<16>", "step_kernel_16x16_partial_traffic.txt"),
+    5: ("nrts::step_kernel_wide<64>", "step_kernel_64x64_traffic.txt"),
+}
+
+
+def load_traffic(workload: str = "random", config: int = 2) -> float | None:
     """DRAM bytes per env-step of the measured kernel from the committed ncu summary."""
-    name = "duel_kernel_16x16_traffic.txt" if workload == "duel" else "step_kernel_16x16_traffic.txt"
+    name = "duel_kernel_16x16_traffic.txt" if workload == "duel" else KERNELS[config][1]
+    if name is None:
+        return None
     path = ROOT / "profiles" / name
     if not path.exists():
         return None
@@ -473,7 +485,7 @@ def main() -> None:
         bytes_per["total"] += bytes_per["sampled_actions"]
     peak, peak_kind = load_peaks()
     achieved = bytes_per["total"] * L / (step_kernel_ms * 1e-3) / 1e9
-    traffic = load_traffic() if args.config == 2 else None
+    traffic = load_traffic("random", args.config)
     if traffic is not None:  # ncu DRAM bytes per env-step -> per launch of L games
         traffic *= L
     line = None
@@ -509,9 +521,9 @@ def main() -> None:
                 "unit": "GB/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
-                "traffic_unit": "DRAM bytes per launch (ncu capture, profiles/step_kernel_16x16.md)",
+                "traffic_unit": f"DRAM bytes per launch (ncu capture, profiles/{KERNELS[args.config][1]})",
                 "algorithmic_bytes_per_launch": bytes_per["total"] * L,
-                "kernel": "nrts::step_kernel",
+                "kernel": KERNELS[args.config][0],
                 "kernel_ms": step_kernel_ms,
                 "bytes_per_env_step": bytes_per["total"],
                 "peak_kind": peak_kind,

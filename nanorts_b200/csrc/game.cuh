@@ -330,6 +330,22 @@ __device__ __forceinline__ void load_scalars(const Params& P, char* slab, int64_
 }
 
 // Global rows -> slab; scalar leaves -> slab scalars.
+// L2 prefetch of a game's State rows and action rows (their 16-byte-aligned
+// parts), issued one game ahead by warps that step several games.
+__device__ __forceinline__ void prefetch_game(const Params& P, int64_t game, int lane) {
+    if (lane < kSlabLeaves) {
+        const char* src = global_row(P, lane, game);
+        const Span sp = split_row(src, P.layout.row_bytes[lane]);
+        if (sp.body) bulk_prefetch_l2(src + sp.head, sp.body);
+    } else if (lane == 16 || lane == 17) {
+        const int64_t span = static_cast<int64_t>(P.capacity) * kActionColumns * 4;
+        const uintptr_t base = reinterpret_cast<uintptr_t>(P.actions[lane - 16]);
+        const uintptr_t begin = (base + game * span + 15) & ~uintptr_t{15};
+        const uintptr_t end = (base + (game + 1) * span) & ~uintptr_t{15};
+        if (end > begin) bulk_prefetch_l2(reinterpret_cast<const void*>(begin), static_cast<uint32_t>(end - begin));
+    }
+}
+
 __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane) {
     const Layout& L = P.layout;
     if (P.mode == kModeStep && (lane == 16 || lane == 17)) {

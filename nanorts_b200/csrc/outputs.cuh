@@ -216,8 +216,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
                                   int64_t game, uint8_t* maps, int32_t* scalars, const Team& T) {
     if (maps != nullptr) {
         uint8_t* base = maps + game * static_cast<int64_t>(G.cells) * kFeatures;
-        auto cell_features = [&](int32_t c, uint32_t& lo, uint32_t& hi) {
-            const uint32_t w = words[c];
+        auto cell_features = [&](int32_t c, uint32_t w, uint32_t& lo, uint32_t& hi) {
             bool shown = true;
             if (P.partial) {
                 const bool seen = (vis[player * G.h + G.y(c)] >> G.x(c)) & 1ull;
@@ -226,14 +225,19 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
             features(w, player, shown, lo, hi);
         };
         if ((G.cells & 7) == 0 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
-            // 8 cells = 48 bytes = three 16-byte stores; two cells fill three words.
+            // 8 cells = 48 bytes = three 16-byte stores; two cells fill three
+            // words.  The 8 cell words come in two 16-byte loads (lanes 32
+            // bytes apart: 2-way bank conflicts instead of 8-way for words).
             for (int32_t c0 = T.tid * 8; c0 < G.cells; c0 += T.size * 8) {
+                const uint4 qa = reinterpret_cast<const uint4*>(words + c0)[0];
+                const uint4 qb = reinterpret_cast<const uint4*>(words + c0)[1];
+                const uint32_t cw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
                 uint32_t w[12];
 #pragma unroll
                 for (int pair = 0; pair < 4; ++pair) {
                     uint32_t lo0, hi0, lo1, hi1;
-                    cell_features(c0 + 2 * pair, lo0, hi0);
-                    cell_features(c0 + 2 * pair + 1, lo1, hi1);
+                    cell_features(c0 + 2 * pair, cw[2 * pair], lo0, hi0);
+                    cell_features(c0 + 2 * pair + 1, cw[2 * pair + 1], lo1, hi1);
                     w[3 * pair] = lo0;
                     w[3 * pair + 1] = hi0 | (lo1 << 16);
                     w[3 * pair + 2] = (lo1 >> 16) | (hi1 << 16);
@@ -246,7 +250,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
         } else {
             for (int32_t c = T.tid; c < G.cells; c += T.size) {
                 uint32_t lo, hi;
-                cell_features(c, lo, hi);
+                cell_features(c, words[c], lo, hi);
                 for (int b = 0; b < 4; ++b) base[c * kFeatures + b] = static_cast<uint8_t>(lo >> (8 * b));
                 base[c * kFeatures + 4] = static_cast<uint8_t>(hi);
                 base[c * kFeatures + 5] = static_cast<uint8_t>(hi >> 8);

@@ -122,11 +122,14 @@ __device__ __forceinline__ bool game_core(const Params& P, const Header& H, cons
     return true;
 }
 
-// One game through the launch's mode on its warp; false when a bounded wait gave up.
+// One game through the launch's mode on its warp; false when a bounded wait
+// gave up.  `next` (>= 0) is the warp's next game, whose rows are pulled into
+// L2 while this game's outputs are written.
 template <int kW>
 __device__ __forceinline__ bool run_game(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
-                                         uint32_t parity, int64_t game, int lane) {
+                                         uint32_t parity, int64_t game, int lane, int64_t next = -1) {
     if (!game_core(P, H, G, slab, bar, parity, game, lane)) return false;
+    if (next >= 0) prefetch_game(P, next, lane);
     const Game g = game_view(P, slab, game);
     write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, warp_team(lane));
     if (P.mode != kModeOutputs) finish_stores(P, lane);
@@ -156,7 +159,9 @@ __device__ __forceinline__ void step_block(const Params& P, int64_t block, int64
     uint32_t parity = 0;
     for (int64_t g0 = block * warps + warp; g0 < P.lanes; g0 += stride) {
         const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
-        if (!run_game(P, H, G, slab, bar, parity, game, lane)) break;
+        const int64_t g1 = g0 + stride;
+        const int64_t next = P.mode == kModeStep && g1 < P.lanes ? (P.reverse ? P.lanes - 1 - g1 : g1) : -1;
+        if (!run_game(P, H, G, slab, bar, parity, game, lane, next)) break;
         if (P.mode != kModeReset) parity ^= 1u;
     }
 }
@@ -207,6 +212,8 @@ __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __g
         if (warp == 0) {
             const bool done = game_core(P, H, G, slab, bar, parity, game, lane);
             if (lane == 0) *ok = done;
+            const int64_t g1 = g0 + gridDim.x;
+            if (done && P.mode == kModeStep && g1 < P.lanes) prefetch_game(P, P.reverse ? P.lanes - 1 - g1 : g1, lane);
         }
         __syncthreads();
         if (!*ok) break;
@@ -619,9 +626,15 @@ int launch_step(Params& P, void* stream) {
     if (L.header_bytes + L.slab_bytes > info->smem_optin) return fail(NRTS_E_ARGUMENT, "one game does not fit in shared memory");
     const bool bots = P.mode == kModeDuel || P.mode == kModeBotAct;
     if (!bots && L.slab_bytes > kWideSlabBytes) {
-        // Few games fit per SM: give each one a CTA of kTeamWarps warps.
+        // Few games fit per SM: give each one a CTA of kTeamWarps warps, on a
+        // persistent grid (each CTA steps every grid-th game and pulls its
+        // next game's rows into L2 while writing the current one's outputs).
         const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
-        const unsigned blocks = static_cast<unsigned>(P.lanes);
+        int resident = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, pick_wide_kernel(P.width), 32 * kTeamWarps, smem) != cudaSuccess ||
+            resident < 1)
+            resident = 1;
+        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(P.lanes, static_cast<int64_t>(info->sms) * resident));
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         switch (P.width) {
             case 8: step_kernel_wide<8><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
