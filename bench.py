@@ -112,6 +112,10 @@ def load_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+# Environment states (each on its own stream) the end-to-end loop splits a
+# GPU's games into.
+E2E_SHARDS = 4
+
 # The kernel each configuration's step launches on a B200 (148 SMs) and the
 # committed ncu summary holding its DRAM bytes per env-step.
 KERNELS = {
@@ -443,25 +447,53 @@ def main() -> None:
     elapsed_ms, step_kernel_ms = timing.tolist()
 
     # End to end through the public API with host buffers: each step copies the
-    # actions from pinned host memory, steps, samples the next actions on the
-    # device and reads the actions, rewards and dones back to the host.
+    # actions from pinned host memory, steps (drawing the next actions on the
+    # device as the timed steps do) and reads the next actions, rewards and
+    # dones back to the host.  The rank's games run as E2E_SHARDS environment
+    # states, each on its own stream, so that one shard's host->device copy
+    # overlaps another's device->host copy (PCIe moves both ways at once).
     C = game.bucket.per_player_capacity
-    host_actions = torch.empty((2, L, C, 7), dtype=torch.int32).pin_memory()
-    host_actions.copy_(torch.stack([a.cpu() for a in env.sample_actions(state, rank, 1).values()]))
-    host_rewards = torch.empty((L, 2), dtype=torch.float32).pin_memory()
-    host_dones = torch.empty((L,), dtype=torch.bool).pin_memory()
-    dev_actions = torch.empty((2, L, C, 7), dtype=torch.int32, device=device)
+    # Small batches (under 32 MB of actions per step) stay one state: there the
+    # per-launch latency outweighs the copy overlap.
+    K = E2E_SHARDS if L % E2E_SHARDS == 0 and L * C * 7 * 4 * 2 >= 32 << 20 else 1
+    per = L // K
+    e2e_keys = shard_keys(all_keys, shard).to(device).view(torch.uint32)
+    streams = [torch.cuda.Stream(device) for _ in range(K)]
+    shards = []
+    for k in range(K):
+        with torch.cuda.stream(streams[k]):
+            _, st = env.reset(e2e_keys[k * per:(k + 1) * per].contiguous())
+            first = env.sample_actions(st, seed=rank, counter=1)
+            sh = {
+                "state": st,
+                "host": torch.empty((2, per, C, 7), dtype=torch.int32).pin_memory(),
+                "dev": torch.empty((2, per, C, 7), dtype=torch.int32, device=device),
+                "rewards": torch.empty((per, 2), dtype=torch.float32).pin_memory(),
+                "dones": torch.empty((per,), dtype=torch.bool).pin_memory(),
+            }
+            sh["host"][0].copy_(first["player_0"])
+            sh["host"][1].copy_(first["player_1"])
+        shards.append(sh)
+    torch.cuda.synchronize(device)
     e2e_steps = args.e2e_steps
 
     def e2e_step(i: int) -> None:
-        dev_actions.copy_(host_actions, non_blocking=True)
-        _, _, rewards, dones, _ = env.step(None, state, {"player_0": dev_actions[0], "player_1": dev_actions[1]})
-        nxt = env.sample_actions(state, seed=rank, counter=2 * 10**9 + i)
-        host_actions[0].copy_(nxt["player_0"], non_blocking=True)
-        host_actions[1].copy_(nxt["player_1"], non_blocking=True)
-        host_rewards.copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
-        host_dones.copy_(dones["__all__"], non_blocking=True)
-        stream.synchronize()
+        for k, sh in enumerate(shards):
+            with torch.cuda.stream(streams[k]):
+                sh["dev"].copy_(sh["host"], non_blocking=True)
+                acts = {"player_0": sh["dev"][0], "player_1": sh["dev"][1]}
+                if fused:
+                    _, _, rewards, dones, infos = env.step(None, sh["state"], acts, sample=(rank, 2 * 10**9 + i))
+                    nxt = infos["sampled_actions"]
+                else:
+                    _, _, rewards, dones, _ = env.step(None, sh["state"], acts)
+                    nxt = env.sample_actions(sh["state"], seed=rank, counter=2 * 10**9 + i)
+                sh["host"][0].copy_(nxt["player_0"], non_blocking=True)
+                sh["host"][1].copy_(nxt["player_1"], non_blocking=True)
+                sh["rewards"].copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
+                sh["dones"].copy_(dones["__all__"], non_blocking=True)
+        for s_k in streams:
+            s_k.synchronize()
 
     for i in range(3):
         e2e_step(i)
@@ -470,8 +502,12 @@ def main() -> None:
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    for s_k in streams:
+        s_k.wait_event(e0)
     for i in range(e2e_steps):
         e2e_step(3 + i)
+    for s_k in streams:
+        stream.wait_stream(s_k)
     e1.record(stream)
     torch.cuda.synchronize(device)
     e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
@@ -534,6 +570,7 @@ def main() -> None:
                 "unit": "env-steps/s",
                 "h2d_bytes_per_step": global_games * C * 7 * 4 * 2,
                 "d2h_bytes_per_step": global_games * C * 7 * 4 * 2 + global_games * (2 * 4 + 1),
+                "shards_per_gpu": K,
             },
             "gpu_launches": (1 if fused else 2) * args.steps,
             "episodes": episode_stats,
