@@ -625,27 +625,41 @@ int launch_step(Params& P, void* stream) {
     const Layout& L = P.layout;
     if (L.header_bytes + L.slab_bytes > info->smem_optin) return fail(NRTS_E_ARGUMENT, "one game does not fit in shared memory");
     const bool bots = P.mode == kModeDuel || P.mode == kModeBotAct;
-    if (!bots && L.slab_bytes > kWideSlabBytes) {
-        // Few games fit per SM: give each one a CTA of kTeamWarps warps, on a
-        // persistent grid (each CTA steps every grid-th game and pulls its
-        // next game's rows into L2 while writing the current one's outputs).
+    if (!bots) {
+        // Team launches: one game per CTA of `team` warps (the warps share the
+        // output phase), on a persistent grid (each CTA steps every grid-th
+        // game and pulls its next game's rows into L2 while writing the
+        // current one's outputs).  Wide boards always take 4-warp teams (few
+        // of their games fit per SM anyway); smaller boards take the widest
+        // team that keeps the whole batch resident at once, when the batch is
+        // that small: their step is then bound by one game's latency.
         const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
-        int resident = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, pick_wide_kernel(P.width), 32 * kTeamWarps, smem) != cudaSuccess ||
-            resident < 1)
-            resident = 1;
-        const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(P.lanes, static_cast<int64_t>(info->sms) * resident));
-        cudaStream_t s = static_cast<cudaStream_t>(stream);
-        switch (P.width) {
-            case 8: step_kernel_wide<8><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
-            case 16: step_kernel_wide<16><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
-            case 32: step_kernel_wide<32><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
-            case 64: step_kernel_wide<64><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
-            default: step_kernel_wide<0><<<blocks, 32 * kTeamWarps, smem, s>>>(P); break;
+        const bool wide = L.slab_bytes > kWideSlabBytes;
+        int team = 0, resident = 0;
+        for (int warps = kTeamWarps; warps >= 2 && team == 0; warps /= 2) {
+            int r = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, pick_wide_kernel(P.width), 32 * warps, smem) != cudaSuccess) r = 0;
+            if (wide || static_cast<int64_t>(r) * info->sms >= P.lanes) {
+                team = warps;
+                resident = std::max(r, 1);
+            }
+            if (wide) break;
         }
-        const cudaError_t err = cudaGetLastError();
-        if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("wide kernel launch: ") + cudaGetErrorString(err));
-        return NRTS_OK;
+        if (team > 0) {
+            const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(P.lanes, static_cast<int64_t>(info->sms) * resident));
+            const int threads = 32 * team;
+            cudaStream_t s = static_cast<cudaStream_t>(stream);
+            switch (P.width) {
+                case 8: step_kernel_wide<8><<<blocks, threads, smem, s>>>(P); break;
+                case 16: step_kernel_wide<16><<<blocks, threads, smem, s>>>(P); break;
+                case 32: step_kernel_wide<32><<<blocks, threads, smem, s>>>(P); break;
+                case 64: step_kernel_wide<64><<<blocks, threads, smem, s>>>(P); break;
+                default: step_kernel_wide<0><<<blocks, threads, smem, s>>>(P); break;
+            }
+            const cudaError_t err = cudaGetLastError();
+            if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("team kernel launch: ") + cudaGetErrorString(err));
+            return NRTS_OK;
+        }
     }
     // Warps per CTA with the most games resident per SM (registers and shared memory).
     const void* kernel = pick_kernel(P.width, bots);

@@ -132,10 +132,12 @@ def test_parity_contested_moves(config_name):
 
 
 @pytest.mark.parametrize("config_name,lanes", [("c2_16x16_random", 4096), ("c1_8x8_both", 4400),
-                                               ("c3_16x16_alternating_partial", 3600)])
+                                               ("c3_16x16_alternating_partial", 3600), ("c2_16x16_random", 2000)])
 def test_parity_full_batches(config_name, lanes):
-    """Batches large enough to fill every SM: the launch that holds one CTA of
-    up to 28 games per SM (a persistent grid)."""
+    """Batches that fill every SM: from about 3400 games on 16 x 16 the launch
+    holds one CTA of up to 28 games per SM (a persistent grid); 2000 games take
+    CTAs of up to 8 games.  (Small batches, as in the other tests, run one game
+    per CTA of 2 or 4 warps.)"""
     stats = run_parity(config_name, lanes=lanes, steps=60, seed=17, max_cycles=40, move_bias=0.3)
     assert stats["episodes"] > 0
 
