@@ -210,7 +210,7 @@ __device__ bool stage_bots(const Params& P, char* slab, int64_t game, uint64_t* 
         copy_edge_in(a.smem, a.global, sa.head);
         copy_edge_in(a.smem + sa.head + sa.body, a.global + sa.head + sa.body, sa.tail);
     }
-    load_scalars(P, slab, game, lane);
+    load_scalars_at_once(P, slab, game, lane);
     load_carries(P, slab, game, lane);
     const bool ok = wait_phase(bar, parity);
     __syncwarp();

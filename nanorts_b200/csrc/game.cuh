@@ -305,7 +305,11 @@ __device__ __forceinline__ void copy_edge_out(char* dst, const char* src, uint32
         if (i < n) dst[i] = static_cast<char>(b[i]);
 }
 
-// The game's scalar leaves -> slab scalars, one per lane.
+// The game's scalar leaves -> slab scalars, one per lane.  The warp-per-game
+// kernels load them one lane after another (each case's load and store run
+// before the next case's): measured on 16x16 with 23 games per SM, that
+// pacing of the stage gives 101 M env-steps/s against 88 M for loading all 13
+// at once, whose launches end on a longer tail of late warps.
 __device__ __forceinline__ void load_scalars(const Params& P, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     int32_t* s = reinterpret_cast<int32_t*>(slab + L.scal_off);
@@ -329,7 +333,38 @@ __device__ __forceinline__ void load_scalars(const Params& P, char* slab, int64_
     }
 }
 
-// Global rows -> slab; scalar leaves -> slab scalars.
+// The same, every lane loading at once (each lane picks its address first):
+// the team and duel kernels' stage is shorter this way (measured: config 5
+// +7.5 %, bot duels +3.4 %).
+__device__ __forceinline__ void load_scalars_at_once(const Params& P, char* slab, int64_t game, int lane) {
+    const Layout& L = P.layout;
+    int32_t* s = reinterpret_cast<int32_t*>(slab + L.scal_off);
+    const int32_t* res = static_cast<const int32_t*>(P.leaf[NRTS_PLAYER_RESOURCES]);
+    const int32_t* ov = static_cast<const int32_t*>(P.leaf[NRTS_SPAWN_OVERFLOW]);
+    const void* src = nullptr;
+    switch (lane) {
+        case kSTime: src = static_cast<const int32_t*>(P.leaf[NRTS_TIME]) + game; break;
+        case kSRes0: src = res + 2 * game; break;
+        case kSRes1: src = res + 2 * game + 1; break;
+        case kSNextBirth: src = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_BIRTH]) + game; break;
+        case kSNextOrder: src = static_cast<const int32_t*>(P.leaf[NRTS_NEXT_PENDING_ORDER]) + game; break;
+        case kSAlt: src = static_cast<const int32_t*>(P.leaf[NRTS_ALTERNATING_CONFLICT_COUNT]) + game; break;
+        case kSGameOver: src = static_cast<const uint8_t*>(P.leaf[NRTS_GAME_OVER]) + game; break;
+        case kSWinner: src = static_cast<const int32_t*>(P.leaf[NRTS_WINNER]) + game; break;
+        case kSOverflow0: src = ov + 2 * game; break;
+        case kSOverflow1: src = ov + 2 * game + 1; break;
+        case kSEpisode: src = P.episode + game; break;
+        case kSRoot0: src = P.root + 2 * game; break;
+        case kSRoot1: src = P.root + 2 * game + 1; break;
+        default: break;
+    }
+    if (src != nullptr) {
+        const int32_t v = lane == kSGameOver ? static_cast<int32_t>(__ldg(static_cast<const uint8_t*>(src)))
+                                             : __ldg(static_cast<const int32_t*>(src));
+        s[lane] = v;
+    }
+}
+
 // L2 prefetch of a game's State rows and action rows (their 16-byte-aligned
 // parts), issued one game ahead by warps that step several games.
 __device__ __forceinline__ void prefetch_game(const Params& P, int64_t game, int lane) {
@@ -346,7 +381,9 @@ __device__ __forceinline__ void prefetch_game(const Params& P, int64_t game, int
     }
 }
 
-__device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane) {
+// Global rows -> slab; scalar leaves -> slab scalars.
+__device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane,
+                            bool scalars_at_once = false) {
     const Layout& L = P.layout;
     if (P.mode == kModeStep && (lane == 16 || lane == 17)) {
         // The game's action rows are read during admission: pull their
@@ -376,7 +413,8 @@ __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t*
             copy_edge_in(dst + sp.head + sp.body, src + sp.head + sp.body, sp.tail);
         }
     }
-    load_scalars(P, slab, game, lane);
+    if (scalars_at_once) load_scalars_at_once(P, slab, game, lane);
+    else load_scalars(P, slab, game, lane);
     const bool ok = wait_phase(bar, parity);
     __syncwarp();
     return ok;

@@ -100,7 +100,7 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
 // when a bounded wait gave up.
 template <int kW>
 __device__ __forceinline__ bool game_core(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
-                                          uint32_t parity, int64_t game, int lane) {
+                                          uint32_t parity, int64_t game, int lane, bool team = false) {
     Game g = game_view(P, slab, game);
     if (P.mode == kModeReset) {
         load_reset(P, slab, game, lane);
@@ -110,7 +110,7 @@ __device__ __forceinline__ bool game_core(const Params& P, const Header& H, cons
             g.s[kSRoot1] = static_cast<int32_t>(P.keys[2 * game + 1]);
         }
         __syncwarp();
-    } else if (!stage_state(P, slab, game, bar, parity, lane)) {
+    } else if (!stage_state(P, slab, game, bar, parity, lane, team)) {
         return false;
     }
 
@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ Pa
 // One CTA per SM holding as many games (one per warp) as its shared memory
 // takes, up to kBigWarps: no per-CTA reserve or header copy is paid more than
 // once per SM, which fits more games per SM than CTAs of at most 8 warps.
-// The grid is persistent (one CTA per SM; each warp steps every
-// (SMs * warps)-th game).
+// The grid is persistent: each warp steps every (SMs * warps)-th game, so the
+// whole GPU sweeps the batch in order (consecutive games' rows are adjacent in
+// every leaf array), and pulls its next game's rows into L2 while writing the
+// current one's outputs.
 constexpr int kBigWarps = 28;
 
 template <int kW>
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __g
     for (int64_t g0 = blockIdx.x; g0 < P.lanes; g0 += gridDim.x) {
         const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
         if (warp == 0) {
-            const bool done = game_core(P, H, G, slab, bar, parity, game, lane);
+            const bool done = game_core(P, H, G, slab, bar, parity, game, lane, true);
             if (lane == 0) *ok = done;
             const int64_t g1 = g0 + gridDim.x;
             if (done && P.mode == kModeStep && g1 < P.lanes) prefetch_game(P, P.reverse ? P.lanes - 1 - g1 : g1, lane);
@@ -318,18 +320,67 @@ __global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Param
 }
 
 // Uniform draw per factor group from mask rows in HBM (nrts_sample_actions).
-__global__ void sample_kernel(int64_t rows, int32_t width, int32_t types, const uint8_t* masks0, const uint8_t* masks1,
-                              int32_t* actions0, int32_t* actions1, uint32_t key) {
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= 2 * rows) return;
-    const int player = t >= rows;
-    const int64_t row = player ? t - rows : t;
-    const uint8_t* m = (player ? masks1 : masks0) + row * width;
-    uint32_t w[3] = {0u, 0u, 0u};
-    for (int32_t i = 0; i < width; ++i) w[i >> 5] |= static_cast<uint32_t>(m[i] != 0) << (i & 31);
+// Standalone draw (nrts_sample_actions): one warp per 32 consecutive mask rows
+// of one player.  The warp reads the rows' bytes as coalesced 16-byte loads,
+// turns each into 16 flag bits (byte != 0) in a shared bit string, then each
+// lane takes its row's width bits from the string and draws as the fused path.
+constexpr int kSampleWarps = 8;
+constexpr int kSampleMaxWidth = 96;
+
+__global__ void __launch_bounds__(32 * kSampleWarps) sample_kernel(int64_t rows, int32_t width, int32_t types,
+                                                                   const uint8_t* masks0, const uint8_t* masks1,
+                                                                   int32_t* actions0, int32_t* actions1, uint32_t key) {
+    __shared__ uint32_t bits[kSampleWarps][kSampleMaxWidth + 1];  // 32 rows x width bits, one spare word
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t chunks = (rows + 31) / 32;
+    const int64_t chunk = static_cast<int64_t>(blockIdx.x) * kSampleWarps + warp;
+    if (chunk >= 2 * chunks) return;
+    const int player = chunk >= chunks;
+    const int64_t r0 = (chunk - player * chunks) * 32;
+    const int32_t n_rows = static_cast<int32_t>(rows - r0 < 32 ? rows - r0 : 32);
+    const uint8_t* src = (player ? masks1 : masks0) + r0 * width;
+    const int32_t n = n_rows * width;  // bytes of this chunk
+    uint16_t* bits16 = reinterpret_cast<uint16_t*>(bits[warp]);
+    auto flags4 = [](uint32_t x) { return ((__vcmpne4(x, 0u) & 0x01010101u) * 0x00204081u) >> 21 & 0xfu; };
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+        for (int32_t j = lane; 16 * j < n; j += 32) {
+            uint32_t f = 0;
+            if (16 * j + 16 <= n) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(src) + j);
+                f = flags4(q.x) | flags4(q.y) << 4 | flags4(q.z) << 8 | flags4(q.w) << 12;
+            } else {
+                for (int32_t b = 0; 16 * j + b < n; ++b) f |= static_cast<uint32_t>(__ldg(src + 16 * j + b) != 0) << b;
+            }
+            bits16[j] = static_cast<uint16_t>(f);
+        }
+    } else {
+        for (int32_t j = lane; 16 * j < n; j += 32) {
+            uint32_t f = 0;
+            for (int32_t b = 0; b < 16 && 16 * j + b < n; ++b) f |= static_cast<uint32_t>(__ldg(src + 16 * j + b) != 0) << b;
+            bits16[j] = static_cast<uint16_t>(f);
+        }
+    }
+    if (lane == 0) bits[warp][kSampleMaxWidth] = 0u;
+    __syncwarp();
+    if (lane >= n_rows) return;
+    // Row `lane`: bits [lane * width, lane * width + width) of the string.
+    auto take = [&](int32_t at) {  // 32 bits from bit `at`
+        const int32_t wi = at >> 5, b = at & 31;
+        return __funnelshift_r(bits[warp][wi], bits[warp][wi + 1], b);
+    };
+    const int32_t at = lane * width;
+    const uint32_t w0 = take(at);
+    const uint32_t w1 = width > 32 ? take(at + 32) : 0u;
+    uint32_t w2 = width > 64 ? take(at + 64) : 0u;
+    uint32_t w1m = w1;
+    if (width < 64) w1m &= width > 32 ? (1u << (width - 32)) - 1u : 0u;
+    if (width < 96) w2 &= width > 64 ? (1u << (width - 64)) - 1u : 0u;
+    const uint32_t w0m = width < 32 ? w0 & ((1u << width) - 1u) : w0;
+    const int64_t row = r0 + lane;
     int32_t a[kActionColumns];
-    draw_row(w[0], w[1], w[2], types, key, static_cast<uint32_t>(t), a);
+    draw_row(w0m, w1m, w2, types, key, static_cast<uint32_t>(player * rows + row), a);
     int32_t* dst = (player ? actions1 : actions0) + row * kActionColumns;
+#pragma unroll
     for (int f = 0; f < kActionColumns; ++f) dst[f] = a[f];
 }
 
@@ -957,8 +1008,11 @@ int nrts_sample_actions(const NrtsExtents* extents, int64_t lanes, const uint8_t
     const int64_t rows = lanes * extents->capacity;
     if (rows == 0) return NRTS_OK;
     const int32_t width = kKinds + 4 * kDirections + extents->types + extents->offsets;
-    sample_kernel<<<static_cast<unsigned>((2 * rows + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        rows, width, extents->types, masks0, masks1, actions0, actions1, sample_key(seed, counter));
+    if (width > kSampleMaxWidth) return fail(NRTS_E_ARGUMENT, "mask rows wider than 96 bits");
+    const int64_t chunks = 2 * ((rows + 31) / 32);
+    sample_kernel<<<static_cast<unsigned>((chunks + kSampleWarps - 1) / kSampleWarps), 32 * kSampleWarps, 0,
+                    static_cast<cudaStream_t>(stream)>>>(rows, width, extents->types, masks0, masks1, actions0, actions1,
+                                                         sample_key(seed, counter));
     const cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? NRTS_OK : fail(NRTS_E_CUDA, cudaGetErrorString(err));
 }

@@ -164,7 +164,7 @@ def test_parity_reward_components(config_name):
     assert stats["components"]["any"] > 0 and stats["components"]["attack"] > 0
 
 
-@pytest.mark.parametrize("config_name", ["c2_16x16_random", "c5_64x64_random"])
+@pytest.mark.parametrize("config_name", ["c2_16x16_random", "c5_64x64_random", "c1_8x8_both"])
 def test_fused_sampler_matches_standalone_and_oracle(config_name):
     """Actions drawn inside nrts_step equal nrts_sample_actions' on the same
     rows, and stepping on them keeps the kernel equal to the oracle."""
@@ -173,7 +173,7 @@ def test_fused_sampler_matches_standalone_and_oracle(config_name):
 
     cfg = CONFIGS[config_name]
     game = cfg.game(200)
-    lanes = 128 if config_name.startswith("c2") else 8
+    lanes = {"c2": 128, "c5": 8, "c1": 13}[config_name[:2]]  # c1: 611 rows, a partial 32-row chunk
     env = make("NanoRTS", scenario=game, final_observation=False)
     orc = Oracle(game, lanes)
     rng = np.random.default_rng(5)
@@ -194,6 +194,47 @@ def test_fused_sampler_matches_standalone_and_oracle(config_name):
         for a in fused:
             assert torch.equal(fused[a], standalone[a]), f"step {t}: fused draw differs for {a}"
         actions = fused
+
+
+def test_standalone_sampler_reads_any_nonzero_byte_at_any_alignment():
+    """nrts_sample_actions: a row byte is legal when nonzero, and mask arrays
+    that do not start on a 16-byte boundary draw the same actions."""
+    import ctypes
+
+    from nanorts_b200.env import _ptr, make
+    from nanorts_b200.runtime import check, library
+
+    game = CONFIGS["c2_16x16_random"].game(100)
+    lanes, C = 37, game.bucket.per_player_capacity
+    env = make("NanoRTS", scenario=game, final_observation=False)
+    rng = np.random.default_rng(3)
+    keys = random_keys(rng, lanes)
+    _, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
+    for t in range(20):
+        env.step(None, state, env.sample_actions(state, seed=1, counter=t))
+    want = {a: v.clone() for a, v in env.sample_actions(state, seed=4, counter=77).items()}
+    masks = env._row_masks(state)
+    width = masks["player_0"].shape[-1]
+
+    def draw(m0, m1):
+        out = torch.empty((2, lanes, C, 7), dtype=torch.int32, device="cuda")
+        check(library().nrts_sample_actions(ctypes.byref(env._extents), lanes, _ptr(m0), _ptr(m1), _ptr(out[0]),
+                                            _ptr(out[1]), 4, 77, env._stream()))
+        return out
+
+    scaled = [(masks[a].view(torch.uint8) * torch.randint(1, 255, masks[a].shape, device="cuda", dtype=torch.uint8)
+               * (masks[a].view(torch.uint8) != 0)).contiguous() for a in ("player_0", "player_1")]
+    got = draw(scaled[0], scaled[1])
+    for p, a in enumerate(("player_0", "player_1")):
+        assert torch.equal(got[p], want[a]), f"nonzero bytes: {a}"
+    n = lanes * C * width
+    for shift in (1, 5, 8):
+        buf = torch.zeros((2, n + 16), dtype=torch.uint8, device="cuda")
+        buf[0, shift:shift + n] = masks["player_0"].reshape(-1).view(torch.uint8)
+        buf[1, shift:shift + n] = masks["player_1"].reshape(-1).view(torch.uint8)
+        got = draw(buf[0, shift:], buf[1, shift:])
+        for p, a in enumerate(("player_0", "player_1")):
+            assert torch.equal(got[p], want[a]), f"shift {shift}: {a}"
 
 
 def pack_rows(rows: np.ndarray, widths: tuple[int, ...]) -> np.ndarray:
