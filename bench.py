@@ -119,7 +119,7 @@ E2E_SHARDS = 4
 # The kernel each configuration's step launches on a B200 (148 SMs) and the
 # committed ncu summary holding its DRAM bytes per env-step.
 KERNELS = {
-    1: ("nrts::step_kernel<8>", None),
+    1: ("nrts::step_kernel_wide<8> (2-warp CTAs)", None),
     2: ("nrts::step_kernel_big<16>", "step_kernel_16x16_traffic.txt"),
     3: ("nrts::step_kernel_big<16>", "step_kernel_16x16_partial_traffic.txt"),
     5: ("nrts::step_kernel_wide<64>", "step_kernel_64x64_traffic.txt"),
