@@ -255,8 +255,10 @@ int nrts_device_status(int device);
 /* Build identity string of this library. */
 const char* nrts_build_id(void);
 
-/* Runs a probe kernel on each listed device and checks warp ballot and
- * shuffle results and that every kernel image loads.  Returns 0 when all pass. */
+/* Runs probe kernels on each listed device and checks warp ballot and
+ * shuffle results, that every kernel image loads, and that a bounded wait on
+ * an mbarrier nothing completes gives up after 1 ms and records the status
+ * word (whose earlier value is then restored).  Returns 0 when all pass. */
 int nrts_self_check(const int32_t* devices, int64_t count);
 
 /* Message of the last failed call on this host thread. */

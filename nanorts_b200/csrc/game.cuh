@@ -272,13 +272,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Waits for the warp's mbarrier phase, bounded in time; on timeout records the
 // status code and waits once more (bounded) for copies still in flight.
-__device__ bool wait_phase(uint64_t* bar, uint32_t parity) {
+__device__ bool wait_phase(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNanoseconds) {
     const uint64_t start = global_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (global_ns() - start > kWaitNanoseconds) {
+        if (global_ns() - start > limit_ns) {
             atomicExch(&g_status, 1);
             const uint64_t again = global_ns();
-            while (!mbar_try_wait(bar, parity) && global_ns() - again < kWaitNanoseconds) {
+            while (!mbar_try_wait(bar, parity) && global_ns() - again < limit_ns) {
             }
             return false;
         }

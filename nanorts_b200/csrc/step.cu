@@ -402,6 +402,20 @@ __global__ void probe_kernel(int32_t* out) {
     out[1 + lane] = shuffled == ((lane + 5) & 31) * 3;
 }
 
+// A wait on an mbarrier that no copy or thread ever completes: it must give
+// up after `limit_ns`, record the status word and return.  This runs the
+// bounded-wait path of every staging wait without any fault.
+__global__ void wait_probe_kernel(int32_t* out, uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    const bool completed = wait_phase(&bar, 0, limit_ns);
+    if (threadIdx.x == 0) out[0] = completed ? 0 : 1;
+}
+
 }  // namespace nrts
 
 // ===========================================================================
@@ -1077,7 +1091,7 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                                  pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_big_kernel(8),
                                  pick_big_kernel(16), pick_big_kernel(32), pick_big_kernel(64), pick_big_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
-                                 reinterpret_cast<const void*>(probe_kernel)};
+                                 reinterpret_cast<const void*>(probe_kernel), reinterpret_cast<const void*>(wait_probe_kernel)};
         for (const void* k : kernels) {
             if (cudaFuncGetAttributes(&attributes, k) != cudaSuccess) {
                 cudaSetDevice(previous);
@@ -1102,6 +1116,26 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                 cudaSetDevice(previous);
                 return fail(NRTS_E_DEVICE, "warp ballot or shuffle returned a wrong value");
             }
+        }
+        // The bounded wait gives up (1 ms) and records the status word; the
+        // word's earlier value is put back so a real failure stays visible.
+        int32_t before = 0, after = 0, gave_up = 0;
+        if (cudaMemcpyFromSymbol(&before, g_status, sizeof(before)) != cudaSuccess || cudaMalloc(&d, sizeof(int32_t)) != cudaSuccess) {
+            cudaSetDevice(previous);
+            return fail(NRTS_E_CUDA, "status word or allocation failed in the self check");
+        }
+        wait_probe_kernel<<<1, 32>>>(d, 1000000ull);
+        cudaError_t werr = cudaMemcpy(&gave_up, d, sizeof(gave_up), cudaMemcpyDeviceToHost);
+        cudaFree(d);
+        if (werr == cudaSuccess) werr = cudaMemcpyFromSymbol(&after, g_status, sizeof(after));
+        if (werr == cudaSuccess) werr = cudaMemcpyToSymbol(g_status, &before, sizeof(before));
+        if (werr != cudaSuccess) {
+            cudaSetDevice(previous);
+            return fail(NRTS_E_CUDA, cudaGetErrorString(werr));
+        }
+        if (gave_up != 1 || after != 1) {
+            cudaSetDevice(previous);
+            return fail(NRTS_E_DEVICE, "a bounded wait did not give up and record its status");
         }
     }
     cudaSetDevice(previous);
