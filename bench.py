@@ -114,7 +114,7 @@ def load_peaks() -> tuple[float, str]:
 
 # Environment states (each on its own stream) the end-to-end loop splits a
 # GPU's games into.
-E2E_SHARDS = 4
+E2E_SHARDS = 8
 
 # The kernel each configuration's step launches on a B200 (148 SMs) and the
 # committed ncu summary holding its DRAM bytes per env-step.
@@ -343,6 +343,8 @@ def main() -> None:
     parser.add_argument("--config", type=int, default=2, choices=(1, 2, 3, 4, 5),
                         help="BASELINE.json config number (1-based); 2 is the headline, 4 selects the duel")
     parser.add_argument("--lanes", type=int, default=None, help="games per GPU")
+    parser.add_argument("--e2e-shards", type=int, default=E2E_SHARDS,
+                        help="environment states (one stream each) the e2e loop splits a GPU's games into")
     parser.add_argument("--impl", default="nanorts_b200", choices=("nanorts_b200", "reference"))
     parser.add_argument("--e2e-steps", type=int, default=50)
     parser.add_argument("--stat-steps", type=int, default=None,
@@ -455,7 +457,7 @@ def main() -> None:
     C = game.bucket.per_player_capacity
     # Small batches (under 32 MB of actions per step) stay one state: there the
     # per-launch latency outweighs the copy overlap.
-    K = E2E_SHARDS if L % E2E_SHARDS == 0 and L * C * 7 * 4 * 2 >= 32 << 20 else 1
+    K = args.e2e_shards if L % args.e2e_shards == 0 and L * C * 7 * 4 * 2 >= 32 << 20 else 1
     per = L // K
     e2e_keys = shard_keys(all_keys, shard).to(device).view(torch.uint32)
     streams = [torch.cuda.Stream(device) for _ in range(K)]
