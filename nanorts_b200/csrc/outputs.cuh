@@ -301,39 +301,22 @@ __device__ __forceinline__ void draw_row(uint32_t w0, uint32_t w1, uint32_t w2, 
 template <int kW>
 __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, const Game& g, uint32_t* words, uint64_t* occ, bool rows,
                                            int32_t entities, const Team& T) {
-    const int32_t lane = T.lane();
     auto word_of = [&](int32_t c) {
         const int32_t s = g.entity_at[c];
         const uint32_t wall_bit = ((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u;
         return (s == kAbsent ? 0u : occupant_word(g, s)) | wall_bit;
     };
-    if constexpr (kW > 0 && kW <= 32) {
-        constexpr int kRowsPerChunk = 32 / kW;
-        constexpr uint32_t kMask = kW == 32 ? ~0u : ((1u << kW) - 1u);
-        for (int32_t base = 32 * T.warp(); base < G.cells; base += T.size) {
-            const int32_t c = base + lane;
-            const uint32_t w = c < G.cells ? word_of(c) : 0u;
-            if (c < G.cells) words[c] = w;
-            const unsigned m0 = __ballot_sync(kFull, ((w >> 28) & 3u) == 1u);
-            const unsigned m1 = __ballot_sync(kFull, ((w >> 28) & 3u) == 2u);
-            if (rows && lane < kRowsPerChunk) {
-                const int32_t row = base / kW + lane;
-                if (row < G.h) {
-                    occ[row] = (m0 >> (lane * kW)) & kMask;
-                    occ[G.h + row] = (m1 >> (lane * kW)) & kMask;
-                }
-            }
-        }
-    } else if constexpr (kW == 64) {
-        // Wide boards hold few units per cell: the wall bits of every cell in
-        // 16-byte groups, then the occupant word of each cell entity_at names,
-        // found from the active slots (entity_at names exactly the active
-        // slots' cells, the State invariant of model/state.py:87-165).
+    if constexpr (kW > 0) {
+        // Boards hold few units per cell: the wall bits of every cell in
+        // 16-byte groups (four cells of one row), then the occupant word of
+        // each cell entity_at names, found from the active slots (entity_at
+        // names exactly the active slots' cells, the State invariant of
+        // model/state.py:87-165).
         if (rows)
             for (int32_t r = T.tid; r < 2 * G.h; r += T.size) occ[r] = 0ull;
         for (int32_t q = T.tid; q < (G.cells >> 2); q += T.size) {
             const int32_t c = q << 2;
-            const uint32_t bits = static_cast<uint32_t>(H.terrain_rows[c >> 6] >> (c & 63)) & 0xfu;
+            const uint32_t bits = static_cast<uint32_t>(H.terrain_rows[c / kW] >> (c % kW)) & 0xfu;
             reinterpret_cast<uint4*>(words)[q] = make_uint4(bits & 1u ? kWallBit : 0u, bits & 2u ? kWallBit : 0u,
                                                             bits & 4u ? kWallBit : 0u, bits & 8u ? kWallBit : 0u);
         }
@@ -346,7 +329,7 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
             words[c] = w;
             const uint32_t code = (w >> 28) & 3u;
             if (rows && (code == 1u || code == 2u))
-                atomicOr(reinterpret_cast<unsigned long long*>(&occ[(code - 1) * G.h + (c >> 6)]), 1ull << (c & 63));
+                atomicOr(reinterpret_cast<unsigned long long*>(&occ[(code - 1) * G.h + c / kW]), 1ull << (c % kW));
         }
     } else {
         if (rows)

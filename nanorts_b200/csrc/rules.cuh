@@ -352,7 +352,8 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
     // opponent minus attacks on own units, combat units.
     int32_t* events = reinterpret_cast<int32_t*>(produce_claims + 2);
     const bool counting = P.out.reward_components != nullptr;
-    for (int32_t i = lane; i < count_words + 2 + 2 * kEventCounts; i += 32) counts[i] = 0u;
+    for (int32_t i = lane; 4 * i < count_words + 2 + 2 * kEventCounts; i += 32)  // the region is 16-byte aligned and padded
+        reinterpret_cast<uint4*>(counts)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
     // One pass over the slots: available owned slots (actions.py:65-75,
     // legality.py:169-170) and the claim holders at the step's start, with
