@@ -67,7 +67,7 @@ struct Layout {
     // Epilogue scratch (aliases both, and `order` when no bots run).
     int32_t word_off;    // uint32 [cells] occupant words
     int32_t rows_off;    // uint64 [4H] occupancy (2) and visibility (2) rows
-    int32_t mask_off;    // uint32 [2C * 3 + 2] legality row words
+    int32_t mask_off;    // uint32 [2C * 3 + 6] legality row words, then up to 4 per-warp counts
     // Scripted bots (duel and bot-act launches only; 0 otherwise).
     int32_t carry_off;   // two players' carries (bots.cuh carry_bytes each)
     int32_t cmd_off;     // command rows of both players (CmdLayout)

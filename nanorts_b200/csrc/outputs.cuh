@@ -384,8 +384,8 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
         // available ones are listed (by the first warp) and computed densely.
         int16_t* avail = reinterpret_cast<int16_t*>(slab + L.list_off);
         int32_t A = 0;
-        if (T.warp() == 0) {
-            const int lane = T.lane();
+        const int lane = T.lane();
+        if (!T.cta()) {
             for (int32_t base = 0; base < P.owned; base += 32) {
                 const int32_t p = base + lane;
                 const bool in = p < P.owned;
@@ -399,10 +399,40 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
                 if (available) avail[A + __popc(m & lanes_below(lane))] = static_cast<int16_t>(p);
                 A += __popc(m);
             }
-            if (T.cta() && lane == 0) rows[3 * P.owned] = static_cast<uint32_t>(A);
+        } else {
+            // Each warp of the CTA lists the available units of its own run
+            // of 32-slot chunks (and writes the others' NONE rows); the
+            // per-warp counts place every run in slot order.
+            const int32_t teams = T.size >> 5, chunks = (P.owned + 31) >> 5, per = (chunks + teams - 1) / teams;
+            const int32_t first = min(chunks, T.warp() * per) * 32, last = min(chunks, (T.warp() + 1) * per) * 32;
+            auto available_at = [&](int32_t p) {
+                return p < P.owned && g.birth[P.neutral + p] != kAbsent && g.pending_kind[P.neutral + p] == kAbsent;
+            };
+            uint32_t* team_counts = rows + 3 * P.owned + 2;  // spare words after the rows
+            int32_t mine = 0;
+            for (int32_t base = first; base < last; base += 32) mine += __popc(__ballot_sync(kFull, available_at(base + lane)));
+            if (lane == 0) team_counts[T.warp()] = static_cast<uint32_t>(mine);
+            T.sync();
+            int32_t at = 0;
+            for (int32_t k = 0; k < teams; ++k) {
+                const int32_t v = static_cast<int32_t>(team_counts[k]);
+                at += k < T.warp() ? v : 0;
+                A += v;
+            }
+            for (int32_t base = first; base < last; base += 32) {
+                const int32_t p = base + lane;
+                const bool available = available_at(p);
+                if (p < P.owned && !available) {
+                    rows[3 * p] = 1u;
+                    rows[3 * p + 1] = 0u;
+                    rows[3 * p + 2] = 0u;
+                }
+                const unsigned m = __ballot_sync(kFull, available);
+                if (available) avail[at + __popc(m & lanes_below(lane))] = static_cast<int16_t>(p);
+                at += __popc(m);
+            }
         }
         T.sync();
-        if (T.cta()) A = static_cast<int32_t>(rows[3 * P.owned]);
         for (int32_t i = T.tid; i < A; i += T.size) {
             const int32_t p = avail[i];
             uint32_t w0, w1, w2;

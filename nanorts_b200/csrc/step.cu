@@ -514,7 +514,7 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     L.word_off = bots ? U : L.order_off;
     L.rows_off = L.word_off + round16(cells * 4);
     L.mask_off = L.rows_off + round16(4 * x->height * 8);
-    const int32_t end_epilogue = L.mask_off + round16((owned * 3 + 2) * 4);
+    const int32_t end_epilogue = L.mask_off + round16((owned * 3 + 2 + 4) * 4);  // + the team counts
     off = std::max(end_admission, std::max(end_completion, end_epilogue));
     if (bots) {
         L.bot_off = U;
