@@ -249,7 +249,9 @@ int nrts_duel_step(const NrtsExtents* extents, const NrtsContent* content, const
                    const NrtsBot* bots, const NrtsOutputs* outputs, void* stream);
 
 /* Status word: the device writes a nonzero code here when a kernel's bounded
- * wait gives up.  Reads it (synchronously), clears it and returns it. */
+ * wait gives up (that game and the rest of its warp's games are then left
+ * unstepped).  Reads and clears it in one atomic swap on the device (the
+ * legacy default stream, synchronously) and returns it. */
 int nrts_device_status(int device);
 
 /* Build identity string of this library. */
@@ -257,8 +259,8 @@ const char* nrts_build_id(void);
 
 /* Runs probe kernels on each listed device and checks warp ballot and
  * shuffle results, that every kernel image loads, and that a bounded wait on
- * an mbarrier nothing completes gives up after 1 ms and records the status
- * word (whose earlier value is then restored).  Returns 0 when all pass. */
+ * an mbarrier nothing completes gives up after 1 ms and records a status of
+ * its own (the status word above is not touched).  Returns 0 when all pass. */
 int nrts_self_check(const int32_t* devices, int64_t count);
 
 /* Message of the last failed call on this host thread. */

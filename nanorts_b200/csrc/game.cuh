@@ -271,12 +271,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Waits for the warp's mbarrier phase, bounded in time; on timeout records the
-// status code and waits once more (bounded) for copies still in flight.
-__device__ bool wait_phase(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNanoseconds) {
+// status code in `status` (the library's status word unless given) and waits
+// once more (bounded) for copies still in flight.
+__device__ bool wait_phase(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitNanoseconds, int32_t* status = nullptr) {
     const uint64_t start = global_ns();
     while (!mbar_try_wait(bar, parity)) {
         if (global_ns() - start > limit_ns) {
-            atomicExch(&g_status, 1);
+            atomicExch(status != nullptr ? status : &g_status, 1);
             const uint64_t again = global_ns();
             while (!mbar_try_wait(bar, parity) && global_ns() - again < limit_ns) {
             }

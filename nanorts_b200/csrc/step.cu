@@ -403,8 +403,9 @@ __global__ void probe_kernel(int32_t* out) {
 }
 
 // A wait on an mbarrier that no copy or thread ever completes: it must give
-// up after `limit_ns`, record the status word and return.  This runs the
-// bounded-wait path of every staging wait without any fault.
+// up after `limit_ns`, record the status in out[1] and return.  This runs the
+// bounded-wait path of every staging wait without any fault, and leaves the
+// library's status word to the step kernels.
 __global__ void wait_probe_kernel(int32_t* out, uint64_t limit_ns) {
     __shared__ __align__(8) uint64_t bar;
     if (threadIdx.x == 0) {
@@ -412,9 +413,13 @@ __global__ void wait_probe_kernel(int32_t* out, uint64_t limit_ns) {
         fence_mbar_init();
     }
     __syncwarp();
-    const bool completed = wait_phase(&bar, 0, limit_ns);
+    const bool completed = wait_phase(&bar, 0, limit_ns, out + 1);
     if (threadIdx.x == 0) out[0] = completed ? 0 : 1;
 }
+
+// Reads and clears the status word in one atomic step.
+__device__ int32_t g_status_taken;
+__global__ void take_status_kernel() { g_status_taken = atomicExch(&g_status, 0); }
 
 }  // namespace nrts
 
@@ -765,14 +770,9 @@ int launch_step(Params& P, void* stream) {
     int warps = best_warps;
     // Smaller CTAs when the batch would not fill every SM twice.
     while (warps > 1 && (P.lanes + warps - 1) / warps < 2 * info->sms) --warps;
-    int per_sm = 1;
-    {
-        const size_t smem_w = L.header_bytes + static_cast<size_t>(warps) * L.slab_bytes;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, warps * 32, smem_w) != cudaSuccess || per_sm < 1) per_sm = 1;
-    }
-    // One game per warp; the kernel's stride loop covers grids smaller than the batch.
-    (void)per_sm;
-    const int64_t blocks = (P.lanes + warps - 1) / warps;
+    // One game per warp, up to the grid limit; the kernels' stride loops cover
+    // a grid smaller than the batch.
+    const int64_t blocks = std::min<int64_t>((P.lanes + warps - 1) / warps, INT32_MAX);
     const size_t smem = L.header_bytes + static_cast<size_t>(warps) * L.slab_bytes;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (P.width) {
@@ -1003,6 +1003,7 @@ int nrts_observe(const NrtsExtents* extents, const NrtsContent* content, const N
 
 int nrts_slot_cells(const NrtsExtents* extents, const NrtsState* state, int64_t lanes, int32_t* cells, void* stream) {
     if (int rc = validate(extents)) return rc;
+    if (lanes < 0) return fail(NRTS_E_ARGUMENT, "negative lane count");
     if (state == nullptr || cells == nullptr || state->leaf[NRTS_BIRTH] == nullptr || state->leaf[NRTS_CELL] == nullptr)
         return fail(NRTS_E_ARGUMENT, "null pointer");
     const int32_t owned = 2 * extents->capacity;
@@ -1018,6 +1019,7 @@ int nrts_slot_cells(const NrtsExtents* extents, const NrtsState* state, int64_t 
 int nrts_sample_actions(const NrtsExtents* extents, int64_t lanes, const uint8_t* masks0, const uint8_t* masks1, int32_t* actions0,
                         int32_t* actions1, uint64_t seed, uint64_t counter, void* stream) {
     if (int rc = validate(extents)) return rc;
+    if (lanes < 0) return fail(NRTS_E_ARGUMENT, "negative lane count");
     if (!masks0 || !masks1 || !actions0 || !actions1) return fail(NRTS_E_ARGUMENT, "null pointer");
     const int64_t rows = lanes * extents->capacity;
     if (rows == 0) return NRTS_OK;
@@ -1068,9 +1070,12 @@ int nrts_device_status(int device) {
     int previous;
     if (cudaGetDevice(&previous) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaGetDevice failed");
     if (cudaSetDevice(device) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaSetDevice failed");
-    int32_t value = 0, zero = 0;
-    cudaError_t err = cudaMemcpyFromSymbol(&value, g_status, sizeof(value));
-    if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    int32_t value = 0;
+    // One thread swaps the word with 0, so a code recorded meanwhile is either
+    // returned now or kept for the next call.
+    take_status_kernel<<<1, 1>>>();
+    cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) err = cudaMemcpyFromSymbol(&value, g_status_taken, sizeof(value));
     cudaSetDevice(previous);
     if (err != cudaSuccess) return fail(NRTS_E_CUDA, cudaGetErrorString(err));
     return value;
@@ -1091,7 +1096,8 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                                  pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_big_kernel(8),
                                  pick_big_kernel(16), pick_big_kernel(32), pick_big_kernel(64), pick_big_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
-                                 reinterpret_cast<const void*>(probe_kernel), reinterpret_cast<const void*>(wait_probe_kernel)};
+                                 reinterpret_cast<const void*>(probe_kernel), reinterpret_cast<const void*>(wait_probe_kernel),
+                                 reinterpret_cast<const void*>(take_status_kernel)};
         for (const void* k : kernels) {
             if (cudaFuncGetAttributes(&attributes, k) != cudaSuccess) {
                 cudaSetDevice(previous);
@@ -1117,23 +1123,24 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                 return fail(NRTS_E_DEVICE, "warp ballot or shuffle returned a wrong value");
             }
         }
-        // The bounded wait gives up (1 ms) and records the status word; the
-        // word's earlier value is put back so a real failure stays visible.
-        int32_t before = 0, after = 0, gave_up = 0;
-        if (cudaMemcpyFromSymbol(&before, g_status, sizeof(before)) != cudaSuccess || cudaMalloc(&d, sizeof(int32_t)) != cudaSuccess) {
+        // The bounded wait gives up (1 ms) and records its status in a word of
+        // its own: the library's status word is not touched.
+        int32_t probe[2] = {0, 0};
+        if (cudaMalloc(&d, sizeof(probe)) != cudaSuccess) {
             cudaSetDevice(previous);
-            return fail(NRTS_E_CUDA, "status word or allocation failed in the self check");
+            return fail(NRTS_E_CUDA, "allocation failed in the self check");
         }
-        wait_probe_kernel<<<1, 32>>>(d, 1000000ull);
-        cudaError_t werr = cudaMemcpy(&gave_up, d, sizeof(gave_up), cudaMemcpyDeviceToHost);
+        cudaError_t werr = cudaMemset(d, 0, sizeof(probe));
+        if (werr == cudaSuccess) {
+            wait_probe_kernel<<<1, 32>>>(d, 1000000ull);
+            werr = cudaMemcpy(probe, d, sizeof(probe), cudaMemcpyDeviceToHost);
+        }
         cudaFree(d);
-        if (werr == cudaSuccess) werr = cudaMemcpyFromSymbol(&after, g_status, sizeof(after));
-        if (werr == cudaSuccess) werr = cudaMemcpyToSymbol(g_status, &before, sizeof(before));
         if (werr != cudaSuccess) {
             cudaSetDevice(previous);
             return fail(NRTS_E_CUDA, cudaGetErrorString(werr));
         }
-        if (gave_up != 1 || after != 1) {
+        if (probe[0] != 1 || probe[1] != 1) {
             cudaSetDevice(previous);
             return fail(NRTS_E_DEVICE, "a bounded wait did not give up and record its status");
         }

@@ -37,7 +37,7 @@ from nanorts_b200.model import (
     UnitTypeTableVersion,
     leaf_shapes,
 )
-from nanorts_b200.runtime import Content, Extents, Outputs, StatePtrs, check, library
+from nanorts_b200.runtime import Content, Extents, Outputs, StatePtrs, check, check_device, library
 
 AGENTS = tuple(f"player_{p}" for p in range(PLAYER_COUNT))
 ALL_AGENTS = "__all__"
@@ -505,6 +505,14 @@ class NanoRTS:
         check(library().nrts_legal_masks(ctypes.byref(self._extents), ctypes.byref(self._content), ctypes.byref(ptrs),
                                          state.lanes, _ptr(buf["masks"][0]), _ptr(buf["masks"][1]), self._stream()))
         return {agent: buf["masks"][p].view(torch.bool) for p, agent in enumerate(self.agents)}
+
+    def check_device(self) -> None:
+        """Waits for this environment's stream and raises DeviceStatusError when
+        a kernel on the device recorded that a bounded staging wait gave up
+        (the status word is read and cleared; it is shared by every call on
+        the device)."""
+        torch.cuda.current_stream(self.device).synchronize()
+        check_device(self.device.index if self.device.index is not None else torch.cuda.current_device())
 
     def invalidate(self, state: EnvironmentState) -> None:
         """Marks cached masks stale after the caller edited the state's leaves."""

@@ -126,6 +126,19 @@ def library() -> ctypes.CDLL:
     return lib
 
 
+class DeviceStatusError(KernelError):
+    """A kernel's bounded wait gave up: the games it had not stepped are stale."""
+
+
+def check_device(device_index: int) -> None:
+    """Reads and clears the device status word (nrts_device_status, synchronous);
+    raises DeviceStatusError when a kernel recorded that a bounded wait gave up."""
+    status = check(library().nrts_device_status(device_index))
+    if status != 0:
+        raise DeviceStatusError(f"device {device_index}: a kernel's bounded wait gave up (status {status}); "
+                                "the games of that launch's remaining warps were not stepped")
+
+
 def check(code: int) -> int:
     if code < 0:
         message = library().nrts_last_error().decode()

@@ -92,12 +92,23 @@ def astar(free: np.ndarray, start: int, target: int, range_: int) -> tuple[bool,
     return bool(out[0]), int(out[1]), int(out[2]), int(out[3])
 
 
+def reference_root() -> Path | None:
+    """Root of a NanoRTS checkout (the directory holding ``src/nanorts``), or None.
+
+    ``NANORTS_REFERENCE`` names it; without the variable a checkout named
+    ``reference`` beside this repository is used when it exists.
+    """
+    named = os.environ.get("NANORTS_REFERENCE")
+    root = Path(named) if named else HERE.parent.parent / "reference"
+    return root if (root / "src" / "nanorts").is_dir() else None
+
+
 def build() -> None:
-    """Compile the oracle (and, where the reference tree exists, its reference builds)."""
-    targets = ["all"]
-    if Path(os.environ.get("NANORTS_REFERENCE", "/root/reference/src/nanorts")).exists():
-        targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    """Compile the oracle (and, where a reference checkout exists, its reference builds)."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "all"], check=True)
+    root = reference_root()
+    if root is not None:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"NANORTS_REFERENCE={root}"], check=True)
 
 
 def _load() -> ctypes.CDLL:
@@ -108,6 +119,8 @@ def _load() -> ctypes.CDLL:
     lib.oracle_env_step.argtypes = [p, p, ctypes.c_int64] + [p] * 17 + [ctypes.c_int]
     lib.oracle_core_step.argtypes = [p, p, ctypes.c_int64, p, p, p, p, p, ctypes.c_int]
     lib.oracle_legal_masks.argtypes = [p, p, ctypes.c_int64, p, p, ctypes.c_int]
+    lib.oracle_decode_actions.argtypes = [p, p, ctypes.c_int64, p, p, p, ctypes.c_int]
+    lib.oracle_visible_cells.argtypes = [p, p, ctypes.c_int64, ctypes.c_int32, p, ctypes.c_int]
     lib.oracle_observe.argtypes = [p, p, ctypes.c_int64, p, p, p, p, ctypes.c_int]
     lib.oracle_reset.argtypes = [p, p, ctypes.c_int64]
     lib.oracle_threefry2x32.argtypes = [ctypes.c_uint32, ctypes.c_uint32, p, p]
@@ -119,7 +132,7 @@ def _load() -> ctypes.CDLL:
     lib.oracle_astar.argtypes = [p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, p]
     lib.oracle_astar.restype = None
     for name in ("oracle_env_step", "oracle_core_step", "oracle_legal_masks", "oracle_observe", "oracle_reset",
-                 "oracle_bot_act", "oracle_duel_step"):
+                 "oracle_bot_act", "oracle_duel_step", "oracle_decode_actions", "oracle_visible_cells"):
         getattr(lib, name).restype = ctypes.c_int
     return lib
 
@@ -204,6 +217,35 @@ class Oracle:
                                       _ptr(masks[1]), self.threads)
         assert rc == 0, rc
         return np.stack(masks, 1)
+
+    def decode_actions(self, actions: np.ndarray) -> np.ndarray:
+        """``decode_actions`` (actions.py:61-84) of int32[L, 2, C, 7] rows: Commands int32[L, 6, 2, C]."""
+        actions = np.ascontiguousarray(actions, np.int32)
+        a0, a1 = np.ascontiguousarray(actions[:, 0]), np.ascontiguousarray(actions[:, 1])
+        commands = np.empty((self.lanes, 6, 2, self.capacity), np.int32)
+        states = self._states()
+        rc = lib().oracle_decode_actions(ctypes.byref(self.config), ctypes.byref(states), self.lanes, _ptr(a0),
+                                         _ptr(a1), _ptr(commands), self.threads)
+        assert rc == 0, rc
+        return commands
+
+    def visible_cells(self, player: int) -> np.ndarray:
+        """Cells ``player`` sees (visibility.py:70-77): bool[L, H, W]."""
+        b = self.game.bucket
+        out = np.empty((self.lanes, b.height, b.width), np.uint8)
+        states = self._states()
+        rc = lib().oracle_visible_cells(ctypes.byref(self.config), ctypes.byref(states), self.lanes, player,
+                                        _ptr(out), self.threads)
+        assert rc == 0, rc
+        return out.astype(bool)
+
+    def episode_roots(self) -> np.ndarray:
+        """``episode_root`` key data per lane (lifecycle.py:34-37): uint32[L, 2]."""
+        out = np.empty((self.lanes, 2), np.uint32)
+        for lane in range(self.lanes):
+            lib().oracle_fold_in(int(self.environment_root[lane, 0]), int(self.environment_root[lane, 1]),
+                                 int(self.episode_index[lane]), out[lane].ctypes.data)
+        return out
 
     def step(self, actions: np.ndarray) -> dict[str, np.ndarray]:
         """The JaxMARL step for actions int32[L, 2, C, 7]."""

@@ -211,6 +211,50 @@ int oracle_core_step(const OracleConfig* c, OracleStates* s, int64_t lanes, cons
     return 0;
 }
 
+// adapters/jaxmarl/actions.py:61-84 decode_actions alone: the Commands
+// int32 [L, 6, 2, C] (kind, direction, none_duration, target_cell,
+// produced_type, request_order) the JaxMARL step hands core.step.
+int oracle_decode_actions(const OracleConfig* c, OracleStates* s, int64_t lanes, const int32_t* actions0,
+                          const int32_t* actions1, int32_t* commands, int threads) {
+    if (int e = check(c)) return e;
+    set_threads(threads);
+    const Extents x = extents_of(c);
+    const int64_t owned = x.owned();
+    const int64_t span = static_cast<int64_t>(x.capacity) * 7;
+#pragma omp parallel for schedule(dynamic, 8)
+    for (int64_t lane = 0; lane < lanes; ++lane) {
+        const Game g = game_at(s->leaf, x, lane);
+        const int32_t* const actions[kPlayers] = {actions0 + lane * span, actions1 + lane * span};
+        const Commands cmd = decode_actions(g, x, actions);
+        int32_t* row = commands + lane * 6 * owned;
+        for (int64_t k = 0; k < owned; ++k) {
+            row[k] = cmd.kind[k];
+            row[owned + k] = cmd.direction[k];
+            row[2 * owned + k] = cmd.none_duration[k];
+            row[3 * owned + k] = cmd.target_cell[k];
+            row[4 * owned + k] = cmd.produced_type[k];
+            row[5 * owned + k] = cmd.request_order[k];
+        }
+    }
+    return 0;
+}
+
+// observations/visibility.py:70-77: uint8 [L, H*W] cells `player` sees (0/1).
+int oracle_visible_cells(const OracleConfig* c, OracleStates* s, int64_t lanes, int32_t player, uint8_t* out, int threads) {
+    if (int e = check(c)) return e;
+    set_threads(threads);
+    const Extents x = extents_of(c);
+    const Content content{c->terrain, c->table, c->types};
+#pragma omp parallel for schedule(dynamic, 8)
+    for (int64_t lane = 0; lane < lanes; ++lane) {
+        const Game g = game_at(s->leaf, x, lane);
+        std::vector<uint8_t> seen;
+        visible_cells(g, content, x, player, seen);
+        std::memcpy(out + lane * x.cells(), seen.data(), seen.size());
+    }
+    return 0;
+}
+
 int oracle_legal_masks(const OracleConfig* c, OracleStates* s, int64_t lanes, uint8_t* masks0, uint8_t* masks1, int threads) {
     if (int e = check(c)) return e;
     set_threads(threads);

@@ -1,0 +1,208 @@
+"""The reference's own CUDA kernels, called through oracle/ref_kernels.cu (TEST INFRASTRUCTURE ONLY).
+
+``make -C oracle ref`` (run by ``oracle.build()`` where a NanoRTS checkout is
+found) compiles NanoRTS's ``nanorts_step``, ``nanorts_legality``,
+``nanorts_legality_words``, ``nanorts_visible_cells`` and
+``nanorts_reset_packed_where_done`` handlers unchanged into
+``oracle/_ref/libref_kernels.so``.  This module hands them torch CUDA tensors
+laid out as the reference's lane-major operands (``kernels/batching.py:64-88``:
+``[L, ...]`` per leaf, a leading 1 for a row every lane shares), so the tests
+can compare the product and the oracle with the reference itself.  Only tests/
+and bench.py's reference arm use it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from nanorts_b200.model import STRATEGY_CODES, UNIT_COLUMNS, GameConfig
+
+HERE = Path(__file__).resolve().parent
+LIBRARY = HERE / "_ref" / "libref_kernels.so"
+
+# Element type codes of the stand-in DataType (ffi_standin/xla/ffi/api/ffi.h).
+_CODES = {torch.bool: 1, torch.int8: 2, torch.int16: 3, torch.int32: 4, torch.uint8: 6}
+U32 = 8
+
+# State leaves in the reference's Leaf order (core/cuda/step.cu:61-85).
+LEAVES = (
+    "birth", "unit_type", "owner", "cell", "hit_points", "carried_resources", "pending_kind", "pending_direction",
+    "pending_none_duration", "pending_target_cell", "pending_produced_type", "pending_issued_at",
+    "pending_completes_at", "pending_order", "entity_at", "time", "player_resources", "next_birth",
+    "next_pending_order", "alternating_conflict_count", "game_over", "winner", "spawn_overflow",
+)
+ROWS = LEAVES[:15]  # per-slot leaves and entity_at: aliased in place by nanorts_step and the reset
+COUNTERS = LEAVES[15:]
+
+# core/unit_tables.py:9-27: the reference kernels' table and timing columns.
+TABLE_COLUMNS = ("can_move", "can_harvest", "is_resource", "is_stockpile", "can_attack", "attack_range", "cost")
+TIMING_COLUMNS = ("move_time", "harvest_time", "attack_time", "produce_time", "hit_points", "attack_damage",
+                  "harvest_amount")
+# core/cycle.py:59-77: event record columns.
+INT32_COLUMNS, INDEX_COLUMNS, INT8_COLUMNS = 6, 4, 6
+TARGET_OWNERS = 3
+
+
+class RefBuffer(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("dtype", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("dims", ctypes.c_int64 * 6)]
+
+
+def available() -> bool:
+    return LIBRARY.exists()
+
+
+_LIB: ctypes.CDLL | None = None
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIBRARY.exists():
+            raise FileNotFoundError(f"{LIBRARY} is not built (make -C oracle ref with NANORTS_REFERENCE set)")
+        ref = ctypes.CDLL(str(LIBRARY))
+        p, i64 = ctypes.c_void_p, ctypes.c_int64
+        ref.ref_step.argtypes = [p, p, i64, p, i64, i64]
+        ref.ref_legality_words.argtypes = [p, p, p, i64]
+        ref.ref_legality_rows.argtypes = [p, p, p]
+        ref.ref_visible_cells.argtypes = [p, p, p, i64, i64, i64, i64]
+        ref.ref_reset_packed_where_done.argtypes = [p, p, p, p, p, i64]
+        for name in ("ref_step", "ref_legality_words", "ref_legality_rows", "ref_visible_cells",
+                     "ref_reset_packed_where_done"):
+            getattr(ref, name).restype = ctypes.c_int
+        ref.ref_last_error.restype = ctypes.c_char_p
+        _LIB = ref
+    return _LIB
+
+
+def describe(t: torch.Tensor, code: int | None = None) -> RefBuffer:
+    assert t.is_contiguous() and t.dim() <= 6
+    b = RefBuffer(data=t.data_ptr(), dtype=_CODES[t.dtype] if code is None else code, rank=t.dim())
+    for k, n in enumerate(t.shape):
+        b.dims[k] = n
+    return b
+
+
+def _array(buffers: list[RefBuffer]):
+    return (RefBuffer * len(buffers))(*buffers)
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what}: {lib().ref_last_error().decode()}")
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class ReferenceKernels:
+    """The reference's kernels for one scenario on the current CUDA device."""
+
+    def __init__(self, game: GameConfig, device: str | torch.device = "cuda") -> None:
+        self.game, b = game, game.bucket
+        self.bucket, self.device = b, torch.device(device)
+        table = game.table
+        col = {name: UNIT_COLUMNS.index(name) for name in UNIT_COLUMNS}
+        T = b.unit_type_capacity
+        ref_table = np.concatenate([table[:, [col[c] for c in TABLE_COLUMNS]], table[:, len(UNIT_COLUMNS):]], axis=1)
+        timings = table[:, [col[c] for c in TIMING_COLUMNS]]
+        dev = self.device
+        self.terrain = torch.from_numpy(np.ascontiguousarray(game.terrain, bool)).reshape(1, b.height, b.width).to(dev)
+        self.table = torch.from_numpy(np.ascontiguousarray(ref_table, np.int32)).reshape(1, T, 7 + T).to(dev)
+        self.timings = torch.from_numpy(np.ascontiguousarray(timings, np.int32)).reshape(1, T, 7).to(dev)
+        self.radius = torch.from_numpy(np.ascontiguousarray(table[:, col["sight_radius"]], np.int32)).reshape(1, T).to(dev)
+        self.strategy = STRATEGY_CODES[b.conflict_strategy]
+
+    # -- nanorts_step ---------------------------------------------------------------------------------------
+    def event_buffers(self, lanes: int) -> list[torch.Tensor]:
+        """The step's 8 event results (core/cycle.py:260-270)."""
+        b, dev = self.bucket, self.device
+        E, T = b.entity_capacity, b.unit_type_capacity
+        i32 = dict(dtype=torch.int32, device=dev)
+        return [
+            torch.empty((lanes, 2), **i32), torch.empty((lanes, 2), **i32), torch.empty((lanes, 2, T), **i32),
+            torch.empty((lanes, 2, TARGET_OWNERS), **i32), torch.empty((lanes, E), dtype=torch.bool, device=dev),
+            torch.empty((lanes, E, INT32_COLUMNS), **i32), torch.empty((lanes, E, INDEX_COLUMNS), dtype=torch.int16, device=dev),
+            torch.empty((lanes, E, INT8_COLUMNS), dtype=torch.int8, device=dev),
+        ]
+
+    def step(self, leaves: dict[str, torch.Tensor], counters_out: dict[str, torch.Tensor], commands: list[torch.Tensor],
+             keys: torch.Tensor, events: list[torch.Tensor]) -> None:
+        """``nanorts_step`` on L games.
+
+        ``leaves``: the 23 State leaves (the row leaves are updated in place);
+        ``counters_out``: result tensors for the 8 counter leaves (time ...
+        spawn_overflow); ``commands``: the six Commands rows, int32 [L, 2, C]
+        each; ``keys``: int32 view of the uint32 [L, 2] random roots.
+        """
+        operands = [describe(keys, U32), *(describe(c) for c in commands), describe(self.terrain), describe(self.table),
+                    describe(self.timings), *(describe(leaves[name]) for name in LEAVES)]
+        results = [*(describe(leaves[name]) for name in ROWS), *(describe(counters_out[name]) for name in COUNTERS),
+                   *(describe(e) for e in events)]
+        _check(lib().ref_step(_stream(), _array(operands), len(operands), _array(results), len(results), self.strategy),
+               "nanorts_step")
+
+    # -- legality -------------------------------------------------------------------------------------------
+    def _legality_operands(self, leaves: dict[str, torch.Tensor]):
+        names = ("birth", "unit_type", "owner", "carried_resources", "cell", "entity_at", "player_resources")
+        return _array([*(describe(leaves[n]) for n in names), describe(self.terrain), describe(self.table)])
+
+    def legality_words(self, leaves: dict[str, torch.Tensor], words: torch.Tensor) -> None:
+        """``nanorts_legality_words``: uint32 [L, 2, C, 3] (given as int32)."""
+        _check(lib().ref_legality_words(_stream(), self._legality_operands(leaves), ctypes.byref(describe(words, U32)),
+                                        self.bucket.attack_offset_capacity), "nanorts_legality_words")
+
+    def legality_rows(self, leaves: dict[str, torch.Tensor], rows: torch.Tensor) -> None:
+        """``nanorts_legality``: bool [L, 2, C, 22 + T + O]."""
+        _check(lib().ref_legality_rows(_stream(), self._legality_operands(leaves), ctypes.byref(describe(rows))),
+               "nanorts_legality")
+
+    def avail_rows(self, leaves: dict[str, torch.Tensor]) -> torch.Tensor:
+        """``legal_actions`` (adapters/jaxmarl/actions.py:28-41) from the words
+        kernel, as the reference's CUDA path assembles it: unpack the words
+        (core/legality.py:148-151), AND ``available`` (legality.py:169-170),
+        rows not available keep only the KIND_NONE bit.  bool [L, 2, C, 78]."""
+        b = self.bucket
+        L, C, N = leaves["birth"].shape[0], b.per_player_capacity, b.neutral_capacity
+        words = torch.empty((L, 2, C, 3), dtype=torch.int32, device=self.device)
+        self.legality_words(leaves, words)
+        shifts = torch.arange(32, device=self.device, dtype=torch.int64)
+        bits = ((words.to(torch.int64) & 0xFFFFFFFF)[..., None] >> shifts) & 1
+        rows = bits.reshape(L, 2, C, 96)[..., : b.mask_width] != 0
+        owned_birth = leaves["birth"][:, N:].reshape(L, 2, C)
+        owned_pending = leaves["pending_kind"][:, N:].reshape(L, 2, C)
+        avail = (owned_birth != -1) & (owned_pending == -1)
+        idle = torch.zeros(b.mask_width, dtype=torch.bool, device=self.device)
+        idle[0] = True
+        return (rows & avail[..., None]) | (~avail[..., None] & idle)
+
+    # -- visibility -----------------------------------------------------------------------------------------
+    def visible_cells(self, leaves: dict[str, torch.Tensor], player: int, out: torch.Tensor) -> None:
+        """``nanorts_visible_cells`` for ``player``'s slot block: bool [L, H, W]."""
+        b = self.bucket
+        operands = _array([describe(leaves["birth"]), describe(leaves["unit_type"]), describe(leaves["cell"]),
+                           describe(self.radius)])
+        first = b.neutral_capacity + player * b.per_player_capacity
+        _check(lib().ref_visible_cells(_stream(), operands, ctypes.byref(describe(out)), first, b.per_player_capacity,
+                                       b.width, b.height), "nanorts_visible_cells")
+
+    # -- auto-reset -----------------------------------------------------------------------------------------
+    def packed_reset_rows(self, reset: dict[str, np.ndarray]) -> torch.Tensor:
+        """One shared uint8 row of the reset State's row leaves, each at the
+        next 16-byte offset (adapters/lifecycle.py:126-137)."""
+        parts = []
+        for name in ROWS:
+            data = np.ascontiguousarray(reset[name]).reshape(-1).view(np.uint8)
+            parts.append(np.pad(data, (0, -data.size % 16)))
+        return torch.from_numpy(np.concatenate(parts)).reshape(1, -1).to(self.device)
+
+    def reset_where_done(self, done: torch.Tensor, packed: torch.Tensor, leaves: dict[str, torch.Tensor]) -> None:
+        """``nanorts_reset_packed_where_done`` in place on the row leaves."""
+        rows = _array([describe(leaves[name]) for name in ROWS])
+        _check(lib().ref_reset_packed_where_done(_stream(), ctypes.byref(describe(done)), ctypes.byref(describe(packed)),
+                                                 rows, rows, len(ROWS)), "nanorts_reset_packed_where_done")

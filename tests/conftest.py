@@ -19,3 +19,20 @@ def oracle_lib():
 
     oracle.build()
     return oracle
+
+
+@pytest.fixture(autouse=True)
+def _device_status_stays_clear(request):
+    """Every GPU test ends with the device status word clear: no kernel's
+    bounded staging wait gave up (a give-up leaves games unstepped)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    from nanorts_b200.runtime import check_device
+
+    torch.cuda.synchronize()
+    check_device(torch.cuda.current_device())

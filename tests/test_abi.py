@@ -149,6 +149,23 @@ def test_null_carry_is_refused(lib):
     assert "carry" in lib.nrts_last_error().decode()
 
 
+def test_negative_lane_counts_are_refused(lib):
+    """nrts_sample_actions and nrts_slot_cells refuse lanes < 0 as every other
+    entry point does, before any launch."""
+    game = map_name_to_scenario("basesWorkers8x8")
+    x = extents_of(game)
+    state, content, keep = _dummy_state_and_content(game)
+    buf = keep[0].ctypes.data
+    assert lib.nrts_sample_actions(ctypes.byref(x), -1, buf, buf, buf, buf, 0, 0, None) == -1
+    assert "negative" in lib.nrts_last_error().decode()
+    assert lib.nrts_slot_cells(ctypes.byref(x), ctypes.byref(state), -3, buf, None) == -1
+    assert "negative" in lib.nrts_last_error().decode()
+    out = runtime.Outputs()
+    assert lib.nrts_step(ctypes.byref(x), ctypes.byref(content), ctypes.byref(state), -2, buf, buf, ctypes.byref(out),
+                         None) == -1
+    assert "negative" in lib.nrts_last_error().decode()
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(runtime, "LIBRARY", tmp_path / "absent.so")
     monkeypatch.setattr(runtime, "_LIB", None)

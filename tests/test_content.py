@@ -3,15 +3,12 @@ initial states (content/normalize.py:45-170, content/scenarios.py:20-42)."""
 
 from __future__ import annotations
 
-from pathlib import Path
-
 import numpy as np
 import pytest
 
 from nanorts_b200 import content, map_name_to_scenario, scenario_names
 from nanorts_b200.model import ConflictStrategy, ModelError, UnitTypeTableVersion
 
-REFERENCE_MAPS = Path("/root/reference/src/nanorts/maps")
 
 
 @pytest.mark.parametrize("name,kw,neutral,capacity,cells", [
@@ -51,10 +48,14 @@ def test_unknown_scenario_is_refused():
 
 
 def test_bundled_maps_match_the_reference_xml():
-    if not REFERENCE_MAPS.exists():
-        pytest.skip("reference map XMLs not present")
+    from oracle.oracle import reference_root
+
+    root = reference_root()
+    if root is None:
+        pytest.skip("no NanoRTS checkout (NANORTS_REFERENCE) to read the map XMLs from")
+    reference_maps = root / "src" / "nanorts" / "maps"
     for name in ("basesWorkers8x8", "basesWorkers16x16", "GardenOfWar64x64", "melee4x4light2"):
-        path = next(REFERENCE_MAPS.rglob(f"{name}.xml"))
+        path = next(reference_maps.rglob(f"{name}.xml"))
         a = content.load_game(path, utt=UnitTypeTableVersion.ORIGINAL, conflict_strategy=ConflictStrategy.CANCEL_RANDOM)
         b = content.map_name_to_scenario(name, utt=UnitTypeTableVersion.ORIGINAL,
                                          conflict_strategy=ConflictStrategy.CANCEL_RANDOM, capacity_profile=False)

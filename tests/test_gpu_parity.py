@@ -67,12 +67,13 @@ def compare_masks(env, env_state, orc, where: str) -> np.ndarray:
 
 
 def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycles: int | None = None,
-               move_bias: float = 0.0, final_observation: bool = True, reward_components: bool = False) -> dict:
+               move_bias: float = 0.0, final_observation: bool = True, reward_components: bool = False,
+               game=None) -> dict:
     from nanorts_b200.env import make
     from oracle.oracle import Oracle
 
     cfg = CONFIGS[config_name]
-    game = cfg.game(max_cycles)
+    game = cfg.game(max_cycles) if game is None else game
     env = make("NanoRTS", scenario=game, partial_observability=cfg.partial, final_observation=final_observation,
                reward_components=reward_components)
     orc = Oracle(game, lanes, partial_observability=cfg.partial, final_observation=final_observation,
@@ -83,7 +84,7 @@ def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycle
     want_obs = orc.reset(keys)
     compare_state(state, orc, "reset")
     compare_obs(obs, want_obs, "reset")
-    episodes = 0
+    episodes, overflowed = 0, 0
     nonzero = {"any": 0, "attack": 0, "win_loss": 0}
     for t in range(steps):
         masks = compare_masks(env, state, orc, f"step {t} masks")
@@ -113,8 +114,9 @@ def run_parity(config_name: str, lanes: int, steps: int, seed: int, *, max_cycle
             nonzero["attack"] += int(np.count_nonzero(want["reward_components"][..., 4]))
             nonzero["win_loss"] += int(np.count_nonzero(want["reward_components"][..., 0]))
         episodes += int(want["done"].sum())
+        overflowed += int((want["spawn_overflow"] > 0).any(axis=1).sum())
     return {"episodes": episodes, "time": orc.state["time"].copy(), "alt": orc.state["alternating_conflict_count"].copy(),
-            "components": nonzero}
+            "components": nonzero, "overflowed": overflowed}
 
 
 @pytest.mark.parametrize("config_name", ["c1_8x8_both", "c2_16x16_random", "c3_16x16_alternating_partial"])
@@ -153,6 +155,74 @@ def test_parity_garden_of_war(config_name):
 def test_parity_long_horizon():
     """Games that run long enough for units to fight and die (default horizon)."""
     run_parity("c2_16x16_random", lanes=48, steps=1200, seed=11, final_observation=False)
+
+
+def test_parity_long_horizon_config3():
+    """Config 3 (fine-tuned table, CANCEL_ALTERNATING, partial observability)
+    at its default horizon: 2000 steps of 64 games."""
+    stats = run_parity("c3_16x16_alternating_partial", lanes=64, steps=2000, seed=23, final_observation=False)
+    print(f"config 3: {stats['episodes']} games ended in 2000 steps")
+    assert stats["alt"].max() > 0
+
+
+def test_parity_long_horizon_config5():
+    """Config 5 (GardenOfWar64x64, CANCEL_RANDOM) for 3000 steps of 8 games."""
+    stats = run_parity("c5_64x64_random", lanes=8, steps=3000, seed=29, final_observation=False, move_bias=0.1)
+    print(f"config 5: {stats['episodes']} games ended in 3000 steps")
+
+
+def test_parity_spawn_overflow():
+    """A player block of 3 slots on basesWorkers8x8: production runs out of
+    slots, the kernel counts spawn_overflow (core/kinds/produce.py:55-75) as
+    the oracle does, and the telemetry turns nonzero."""
+    from nanorts_b200.content import assemble_game, shipped_document
+    from nanorts_b200.model import ConflictStrategy, UnitTypeTableVersion
+
+    game = assemble_game(shipped_document("basesWorkers8x8"), utt=UnitTypeTableVersion.ORIGINAL,
+                         conflict_strategy=ConflictStrategy.CANCEL_BOTH, max_cycles=400, per_player_capacity=3)
+    assert game.bucket.per_player_capacity == 3
+    stats = run_parity("c1_8x8_both", lanes=48, steps=500, seed=37, move_bias=0.6, game=game)
+    print(f"spawn overflow: {stats['overflowed']} game-steps with a nonzero counter")
+    assert stats["overflowed"] > 0
+
+
+def test_parity_garden_of_war_production_shape():
+    """Config 5's launch as the benchmark runs it: 1,500 GardenOfWar64x64
+    games on the persistent grid of step_kernel_wide<64> (3 CTAs per SM, 444
+    on a B200, so every CTA steps about 3 games and prefetches the next one
+    into L2), the fused draw on, the game order reversed every other launch,
+    and a horizon of 20 so every game resets inside the run.  (On 8x8 and
+    16x16 boards a team launch is chosen only when the whole batch is
+    resident at once, so games never outnumber CTAs there.)"""
+    from nanorts_b200.env import make
+    from oracle.oracle import Oracle
+
+    cfg = CONFIGS["c5_64x64_random"]
+    game = cfg.game(20)
+    lanes = 1500
+    env = make("NanoRTS", scenario=game, final_observation=False)
+    orc = Oracle(game, lanes)
+    rng = np.random.default_rng(41)
+    keys = random_keys(rng, lanes)
+    obs, state = env.reset(torch.from_numpy(keys.view(np.int32)).cuda().view(torch.uint32))
+    compare_obs(obs, orc.reset(keys), "reset")
+    actions = env.sample_actions(state, seed=3, counter=0)
+    episodes = 0
+    for t in range(30):
+        host = np.stack([_np(actions[a]) for a in ("player_0", "player_1")], 1)
+        want = orc.step(host)
+        obs, state, rewards, dones, infos = env.step(None, state, {a: actions[a].clone() for a in actions},
+                                                     sample=(3, t + 1))
+        where = f"production shape step {t}"
+        compare_state(state, orc, where)
+        compare_obs(obs, want, where)
+        assert np.array_equal(_np(dones["__all__"]), want["done"]), f"{where}: done"
+        assert np.array_equal(_np(rewards["player_0"]), want["reward"][:, 0]), f"{where}: reward"
+        if t % 10 == 9:
+            compare_masks(env, state, orc, where)
+        episodes += int(want["done"].sum())
+        actions = {a: infos["sampled_actions"][a].clone() for a in ("player_0", "player_1")}
+    assert episodes >= lanes
 
 
 @pytest.mark.parametrize("config_name", ["c2_16x16_random", "c1_8x8_both"])
