@@ -2,8 +2,8 @@
 // inside jaxlib) that NanoRTS's kernel sources name.  TEST INFRASTRUCTURE.
 //
 // jaxlib is not installed here, so the reference's .cu files (core/cuda/step.cu,
-// core/cuda/legality.cu, observations/cuda/visibility.cu, adapters/cuda/reset.cu)
-// cannot include the real header.  This file declares the types those files
+// core/cuda/legality.cu, observations/cuda/visibility.cu, adapters/cuda/reset.cu,
+// bots/cuda/abstraction_act.cu) cannot include the real header.  This file declares the types those files
 // use -- buffers, errors, ErrorOr, the remaining-argument lists, the handler
 // macro -- with the same names and member functions, so the reference sources
 // compile unchanged.  XLA_FFI_DEFINE_HANDLER_SYMBOL does not register an XLA
@@ -68,12 +68,13 @@ struct Dimensions {
 };
 
 // A device buffer as a handler sees it: data pointer, element type, extents.
+// As in XLA, the extents live outside the buffer object (in the caller's
+// descriptor, valid for the whole call), so a view taken from a temporary
+// copy of the buffer stays valid.
 class AnyBuffer {
   public:
     AnyBuffer() = default;
-    AnyBuffer(void* data, DataType type, const int64_t* dims, size_t rank) : data_(data), type_(type), rank_(rank) {
-        for (size_t k = 0; k < rank && k < kMaxRank; ++k) dims_[k] = dims[k];
-    }
+    AnyBuffer(void* data, DataType type, const int64_t* dims, size_t rank) : data_(data), type_(type), dims_(dims), rank_(rank) {}
     DataType element_type() const { return type_; }
     Dimensions dimensions() const { return Dimensions{dims_, rank_}; }
     size_t element_count() const {
@@ -85,10 +86,9 @@ class AnyBuffer {
     void* untyped_data() const { return data_; }
 
   private:
-    static constexpr size_t kMaxRank = 8;
     void* data_ = nullptr;
     DataType type_ = DataType::INVALID;
-    int64_t dims_[kMaxRank] = {};
+    const int64_t* dims_ = nullptr;
     size_t rank_ = 0;
 };
 

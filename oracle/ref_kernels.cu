@@ -6,6 +6,7 @@
 //   core/cuda/legality.cu          nanorts_legality(_words) (legality.cu:535-561, kernel :344-378)
 //   observations/cuda/visibility.cu nanorts_visible_cells  (visibility.cu:86-141, kernel :21-71)
 //   adapters/cuda/reset.cu         nanorts_reset_packed_where_done (reset.cu:196-221, kernel :42-80)
+//   bots/cuda/abstraction_act.cu   nanorts_abstraction_act (abstraction_act.cu:1232-1322, kernel :1099)
 // against the interface stand-in in ffi_standin/ (jaxlib, which ships the real
 // XLA FFI header, is absent).  Each handler's XLA_FFI_DEFINE_HANDLER_SYMBOL
 // there exports the address of its implementation function; the entry points
@@ -44,6 +45,7 @@ void* nanorts_legality_implementation(void);
 void* nanorts_legality_words_implementation(void);
 void* nanorts_visible_cells_implementation(void);
 void* nanorts_reset_packed_where_done_implementation(void);
+void* nanorts_abstraction_act_implementation(void);
 }
 
 // A device buffer described by the caller: element type code of the
@@ -86,6 +88,7 @@ using RowsFn = ffi::Error (*)(cudaStream_t, ffi::AnyBuffer, ffi::AnyBuffer, ffi:
                               std::string_view);
 using VisibleFn = ffi::Error (*)(cudaStream_t, ffi::AnyBuffer, ffi::AnyBuffer, ffi::AnyBuffer, ffi::AnyBuffer,
                                  ffi::Result<ffi::AnyBuffer>, std::string_view, int64_t, int64_t, int64_t, int64_t);
+using ActFn = ffi::Error (*)(cudaStream_t, ffi::RemainingArgs, ffi::RemainingRets, std::string_view, int64_t, int64_t);
 using ResetFn = ffi::Error (*)(cudaStream_t, ffi::Buffer<ffi::PRED>, ffi::AnyBuffer, ffi::RemainingArgs, ffi::RemainingRets,
                                std::string_view, int64_t);
 
@@ -146,6 +149,18 @@ int ref_reset_packed_where_done(void* stream, const RefBuffer* done, const RefBu
     return finish(fn(static_cast<cudaStream_t>(stream), ffi::Buffer<ffi::PRED>(any(*done)), any(*packed),
                      ffi::RemainingArgs(args.data(), args.size()), ffi::RemainingRets(rets.data(), rets.size()),
                      nanorts::build_id(), count));
+}
+
+// nanorts_abstraction_act: operands are the ten State leaves the bots read
+// (bots/whole_act.py:22-33), terrain, the bot unit table [1, T, 6], the player
+// [1], then the carry (nine int32 [L, C] rows, trained, next_order); results
+// are the carry (aliased) and the Commands int32 [L, 6, 2, C].
+int ref_abstraction_act(void* stream, const RefBuffer* operands, int64_t n_operands, const RefBuffer* results,
+                        int64_t n_results, int64_t strategy, int64_t trained) {
+    const std::vector<ffi::AnyBuffer> args = all(operands, n_operands), rets = all(results, n_results);
+    const ActFn fn = reinterpret_cast<ActFn>(nanorts_abstraction_act_implementation());
+    return finish(fn(static_cast<cudaStream_t>(stream), ffi::RemainingArgs(args.data(), args.size()),
+                     ffi::RemainingRets(rets.data(), rets.size()), nanorts::build_id(), strategy, trained));
 }
 
 }  // extern "C"

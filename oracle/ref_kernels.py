@@ -2,8 +2,9 @@
 
 ``make -C oracle ref`` (run by ``oracle.build()`` where a NanoRTS checkout is
 found) compiles NanoRTS's ``nanorts_step``, ``nanorts_legality``,
-``nanorts_legality_words``, ``nanorts_visible_cells`` and
-``nanorts_reset_packed_where_done`` handlers unchanged into
+``nanorts_legality_words``, ``nanorts_visible_cells``,
+``nanorts_reset_packed_where_done`` and ``nanorts_abstraction_act`` handlers
+unchanged into
 ``oracle/_ref/libref_kernels.so``.  This module hands them torch CUDA tensors
 laid out as the reference's lane-major operands (``kernels/batching.py:64-88``:
 ``[L, ...]`` per leaf, a leading 1 for a row every lane shares), so the tests
@@ -42,6 +43,12 @@ COUNTERS = LEAVES[15:]
 TABLE_COLUMNS = ("can_move", "can_harvest", "is_resource", "is_stockpile", "can_attack", "attack_range", "cost")
 TIMING_COLUMNS = ("move_time", "harvest_time", "attack_time", "produce_time", "hit_points", "attack_damage",
                   "harvest_amount")
+# bots/whole_act.py:22-42: the State leaves and unit-table columns the bots read.
+BOT_LEAVES = ("birth", "unit_type", "owner", "cell", "carried_resources", "pending_kind", "pending_direction",
+              "pending_produced_type", "entity_at", "player_resources")
+BOT_TABLE_COLUMNS = ("can_harvest", "is_resource", "is_stockpile", "can_attack", "attack_range", "cost")
+# bots/abstraction.py:71-82: the carry's int32 rows, then trained and next_order.
+CARRY_FIELDS = ("kind", "unit_birth", "order", "target", "target_birth", "base", "base_birth", "cell", "unit_type")
 # core/cycle.py:59-77: event record columns.
 INT32_COLUMNS, INDEX_COLUMNS, INT8_COLUMNS = 6, 4, 6
 TARGET_OWNERS = 3
@@ -71,8 +78,9 @@ def lib() -> ctypes.CDLL:
         ref.ref_legality_rows.argtypes = [p, p, p]
         ref.ref_visible_cells.argtypes = [p, p, p, i64, i64, i64, i64]
         ref.ref_reset_packed_where_done.argtypes = [p, p, p, p, p, i64]
+        ref.ref_abstraction_act.argtypes = [p, p, i64, p, i64, i64, i64]
         for name in ("ref_step", "ref_legality_words", "ref_legality_rows", "ref_visible_cells",
-                     "ref_reset_packed_where_done"):
+                     "ref_reset_packed_where_done", "ref_abstraction_act"):
             getattr(ref, name).restype = ctypes.c_int
         ref.ref_last_error.restype = ctypes.c_char_p
         _LIB = ref
@@ -116,6 +124,8 @@ class ReferenceKernels:
         self.table = torch.from_numpy(np.ascontiguousarray(ref_table, np.int32)).reshape(1, T, 7 + T).to(dev)
         self.timings = torch.from_numpy(np.ascontiguousarray(timings, np.int32)).reshape(1, T, 7).to(dev)
         self.radius = torch.from_numpy(np.ascontiguousarray(table[:, col["sight_radius"]], np.int32)).reshape(1, T).to(dev)
+        bot_table = table[:, [col[c] for c in BOT_TABLE_COLUMNS]]
+        self.bot_table = torch.from_numpy(np.ascontiguousarray(bot_table, np.int32)).reshape(1, T, 6).to(dev)
         self.strategy = STRATEGY_CODES[b.conflict_strategy]
 
     # -- nanorts_step ---------------------------------------------------------------------------------------
@@ -206,3 +216,149 @@ class ReferenceKernels:
         rows = _array([describe(leaves[name]) for name in ROWS])
         _check(lib().ref_reset_packed_where_done(_stream(), ctypes.byref(describe(done)), ctypes.byref(describe(packed)),
                                                  rows, rows, len(ROWS)), "nanorts_reset_packed_where_done")
+
+    # -- rush bots ------------------------------------------------------------------------------------------
+    def bot_act(self, leaves: dict[str, torch.Tensor], player: int, strategy: int, trained: int,
+                carry: dict[str, torch.Tensor]) -> torch.Tensor:
+        """``nanorts_abstraction_act`` for one player's rush bot: updates the
+        carry (CARRY_FIELDS int32 [L, C], ``trained`` 0/1 uint8 [L, C],
+        ``next_order`` int32 [L]) in place, returns Commands int32 [L, 6, 2, C]."""
+        b = self.bucket
+        L = leaves["birth"].shape[0]
+        who = torch.tensor([player], dtype=torch.int32, device=self.device)
+        carried = [*(describe(carry[n]) for n in CARRY_FIELDS), describe(carry["trained"], _CODES[torch.bool]),
+                   describe(carry["next_order"])]
+        operands = [*(describe(leaves[n]) for n in BOT_LEAVES), describe(self.terrain), describe(self.bot_table),
+                    describe(who), *carried]
+        commands = torch.empty((L, 6, 2, b.per_player_capacity), dtype=torch.int32, device=self.device)
+        results = [*carried, describe(commands)]
+        _check(lib().ref_abstraction_act(_stream(), _array(operands), len(operands), _array(results), len(results),
+                                         strategy, trained), "nanorts_abstraction_act")
+        return commands
+
+
+def sample_uniform(rows: torch.Tensor, widths: tuple[int, ...], generator: torch.Generator | None = None) -> torch.Tensor:
+    """One legal value per factor, uniform over the factor's set bits (0 when
+    none): bool [..., 78] rows -> int32 [..., 7].  The torch form of the
+    oracle's ``sample_uniform_legal``: the stand-in for the reference
+    benchmark's per-factor ``jax.random.categorical`` over masked logits."""
+    out = []
+    start = 0
+    for width in widths:
+        group = rows[..., start:start + width]
+        count = group.sum(-1)
+        u = torch.rand(count.shape, device=rows.device, generator=generator)
+        pick = torch.floor(u * count.clamp(min=1)).to(torch.int64)
+        chosen = torch.argmax((group.cumsum(-1) > pick[..., None]).to(torch.int8), -1)
+        out.append(torch.where(count > 0, chosen, torch.zeros_like(chosen)))
+        start += width
+    return torch.stack(out, -1).to(torch.int32)
+
+
+def decode_actions(leaves: dict[str, torch.Tensor], actions: torch.Tensor, bucket) -> list[torch.Tensor]:
+    """``decode_actions`` (adapters/jaxmarl/actions.py:61-84, factors.py:117-151)
+    in torch: int32 [L, 2, C, 7] rows -> the six Commands rows int32 [L, 2, C]
+    (kind, direction, none_duration, target_cell, produced_type, request_order).
+    This is the XLA fusion the reference runs before ``nanorts_step``."""
+    L = actions.shape[0]
+    N, C, W, H = bucket.neutral_capacity, bucket.per_player_capacity, bucket.width, bucket.height
+    side = int(round(bucket.attack_offset_capacity ** 0.5))
+    radius = (side - 1) // 2
+    birth = leaves["birth"][:, N:].reshape(L, 2, C)
+    pending = leaves["pending_kind"][:, N:].reshape(L, 2, C)
+    cell = leaves["cell"][:, N:].reshape(L, 2, C).to(torch.int32)
+    available = (birth != -1) & (pending == -1)
+    a = actions.to(torch.int32)
+    kind = torch.where(available, a[..., 0], -1)
+    by_kind = torch.gather(a[..., :5], -1, kind.clamp(0, 4).to(torch.int64)[..., None])[..., 0]
+    direction = torch.where((kind >= 1) & (kind <= 4), by_kind, -1)
+    produced = torch.where(kind == 4, a[..., 5], -1)
+    offset = a[..., 6]
+    tx = torch.remainder(cell, W) + (torch.remainder(offset, side) - radius)
+    ty = torch.div(cell, W, rounding_mode="floor") + (torch.div(offset, side, rounding_mode="floor") - radius)
+    on_board = (tx >= 0) & (tx < W) & (ty >= 0) & (ty < H)
+    target = torch.where((kind == 5) & on_board, ty * W + tx, -1)
+    none_duration = torch.where(kind == 0, 1, 0).to(torch.int32)
+    order = torch.full_like(kind, -1)
+    return [t.to(torch.int32).contiguous() for t in (kind, direction, none_duration, target, produced, order)]
+
+
+class ReferencePath:
+    """The reference's CUDA path for ``NanoRTS.step`` + ``get_avail_actions``
+    on L games: its kernels ``nanorts_step``, ``nanorts_reset_packed_where_done``,
+    ``nanorts_legality_words`` and (partial observability) two
+    ``nanorts_visible_cells`` per step, with torch standing in for the XLA
+    fusions between them (action sampling, ``decode_actions``, the lifecycle's
+    select of the counter leaves, mask assembly).  Only the reference kernels
+    are timed; the feature maps (an XLA fusion in the reference) are not
+    computed, which favours the reference."""
+
+    def __init__(self, game: GameConfig, lanes: int, *, partial: bool = False, seed: int = 0,
+                 device: str | torch.device = "cuda") -> None:
+        from nanorts_b200.content import decide
+
+        self.ref = ReferenceKernels(game, device)
+        self.game, self.lanes, self.partial, self.device = game, lanes, partial, torch.device(device)
+        b = game.bucket
+        reset = decide(game.initial_state, b)
+        self.packed = self.ref.packed_reset_rows(reset)
+        self.reset_rows = {n: torch.from_numpy(np.ascontiguousarray(reset[n])).to(self.device) for n in LEAVES}
+        self.leaves = {n: v.expand(lanes, *v.shape).contiguous() for n, v in self.reset_rows.items()}
+        self.counters = {n: torch.empty_like(self.leaves[n]) for n in COUNTERS}
+        self.events = self.ref.event_buffers(lanes)
+        self.generator = torch.Generator(device=self.device)
+        self.generator.manual_seed(seed)
+        self.keys = torch.randint(-2**31, 2**31 - 1, (lanes, 2), dtype=torch.int32, device=self.device,
+                                  generator=self.generator)
+        self.widths = (6, 4, 4, 4, 4, b.unit_type_capacity, b.attack_offset_capacity)
+        self.words = torch.empty((lanes, 2, b.per_player_capacity, 3), dtype=torch.int32, device=self.device)
+        self.seen = torch.empty((lanes, b.height, b.width), dtype=torch.bool, device=self.device)
+        self.kernel_ms: list[float] = []
+
+    def _rows(self) -> torch.Tensor:
+        b = self.game.bucket
+        L, C, N = self.lanes, b.per_player_capacity, b.neutral_capacity
+        shifts = torch.arange(32, device=self.device, dtype=torch.int64)
+        bits = ((self.words.to(torch.int64) & 0xFFFFFFFF)[..., None] >> shifts) & 1
+        rows = bits.reshape(L, 2, C, 96)[..., : b.mask_width] != 0
+        avail = (self.leaves["birth"][:, N:].reshape(L, 2, C) != -1) & (self.leaves["pending_kind"][:, N:].reshape(L, 2, C) == -1)
+        rows = rows & avail[..., None]
+        rows[..., 0] |= ~avail
+        return rows
+
+    def step(self, timed: bool = True, actions: torch.Tensor | None = None) -> torch.Tensor:
+        """One env step of every game; appends the summed reference-kernel
+        time (CUDA events on the current stream) to ``kernel_ms``.  Draws the
+        actions from the step's masks unless ``actions`` (int32 [L, 2, C, 7])
+        are given; returns the masks (bool [L, 2, C, 78]) the step drew from."""
+        stream = torch.cuda.current_stream(self.device)
+        marks = []
+
+        def run(call):
+            if timed:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call()
+                b.record(stream)
+                marks.append((a, b))
+            else:
+                call()
+
+        run(lambda: self.ref.legality_words(self.leaves, self.words))  # the masks of this step's state
+        if self.partial:
+            for p in range(2):
+                run(lambda p=p: self.ref.visible_cells(self.leaves, p, self.seen))
+        rows = self._rows()
+        if actions is None:
+            actions = sample_uniform(rows, self.widths, self.generator)
+        commands = decode_actions(self.leaves, actions, self.game.bucket)
+        run(lambda: self.ref.step(self.leaves, self.counters, commands, self.keys, self.events))
+        done = self.counters["game_over"] | (self.counters["time"] >= self.game.max_cycles)
+        run(lambda: self.ref.reset_where_done(done, self.packed, self.leaves))
+        for n in COUNTERS:  # lifecycle.py:116-124: the counters take the reset State's values by select
+            shape = (-1,) + (1,) * (self.counters[n].dim() - 1)
+            self.leaves[n].copy_(torch.where(done.view(shape), self.reset_rows[n], self.counters[n]))
+        if timed:
+            torch.cuda.synchronize(self.device)
+            self.kernel_ms.append(sum(a.elapsed_time(b) for a, b in marks))
+        return rows

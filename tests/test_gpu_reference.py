@@ -1,9 +1,9 @@
 """Parity pinned to the reference itself: NanoRTS's own CUDA kernels (needs a B200).
 
 ``oracle/_ref/libref_kernels.so`` holds the reference's ``nanorts_step``,
-``nanorts_legality_words``, ``nanorts_visible_cells`` and
-``nanorts_reset_packed_where_done`` handlers, compiled unchanged from the
-reference sources (``oracle/ref_kernels.cu``).  Along a recorded trajectory of
+``nanorts_legality_words``, ``nanorts_visible_cells``,
+``nanorts_reset_packed_where_done`` and ``nanorts_abstraction_act`` handlers,
+compiled unchanged from the reference sources (``oracle/ref_kernels.cu``).  Along a recorded trajectory of
 uniform legal play (move-biased, so claims collide) every step checks:
 
 * the reference's core step (its kernel, fed the Commands ``decode_actions``
@@ -14,7 +14,9 @@ uniform legal play (move-biased, so claims collide) every step checks:
 * the reference's visible cells (partial observability) against the oracle's;
 * the reference's auto-reset kernel against the oracle's reset rows;
 * the product's ``nrts_step`` against the reference's step on every game the
-  step did not end (an ended game is reset in place by ``nrts_step``).
+  step did not end (an ended game is reset in place by ``nrts_step``);
+* config 4's rush bots: the reference's bot kernel against the oracle's and
+  the product's Commands and carries.
 """
 
 from __future__ import annotations
@@ -151,3 +153,79 @@ def test_reference_kernels_long_horizon():
     """Default horizon, uniform play: fights, deaths and game ends."""
     stats = run_reference_parity("c2_16x16_random", 32, 900, seed=5, max_cycles=5000, move_bias=0.0)
     assert stats is not None
+
+
+@pytest.mark.parametrize("config", ["c4_16x16_both", "obstacle8x8_random", "letmeout_alternating", "itsnotsafe_both",
+                                    "fourbases12_random"])
+def test_reference_bot_kernel_pins_oracle_and_product(config):
+    """Config 4's rush bots: the reference's ``nanorts_abstraction_act`` kernel
+    (WorkerRush for player 0, LightRush for player 1) against the oracle's
+    ``bot_act`` and the product's ``nrts_bot_act``: the Commands and the
+    settled carry of both players at every step of bot-against-bot play, from
+    fresh resets and from random-play prefixes (walls, corridors, a 15-wide
+    board and four bases among the maps)."""
+    ref_kernels = _reference()
+    from nanorts_b200.bots import Bot
+    from nanorts_b200.env import make
+    from oracle.oracle import empty_carry
+    from tests.test_gpu_bots import BOT_CONFIGS, PAIRS, _carry_to_gpu, _compare_carry, _oracle_batch
+    from tests.test_gpu_bots import _upload as upload_env
+
+    cfg = BOT_CONFIGS[config]
+    game = cfg.game(5000 if config.startswith("c4") else 400)
+    bots = PAIRS["worker_vs_light"]
+    orc = _oracle_batch(game, [(8, 0), (8, 20), (16, 60)], seed=19)
+    L, C = orc.lanes, game.bucket.per_player_capacity
+    ref = ref_kernels.ReferenceKernels(game)
+    env = make("NanoRTS", scenario=game, final_observation=False)
+    _, state = env.reset(torch.zeros((L, 2), dtype=torch.int32, device="cuda").view(torch.uint32))
+    gpu_bots = [Bot(f"p{p}", s, t) for p, (s, t) in enumerate(bots)]
+    carries = (empty_carry(L, C), empty_carry(L, C))
+    ended = 0
+    for step in range(500 if config.startswith("c4") else 200):
+        leaves = _upload(orc.state)
+        upload_env(state, orc)
+        env.invalidate(state)
+        for p in range(2):
+            where = f"{config} step {step} player {p}"
+            want_carry = {k: v.copy() for k, v in carries[p].items()}
+            want = orc.bot_act(p, bots[p][0], bots[p][1], want_carry)
+            ref_carry = {k: torch.from_numpy(v.copy()).cuda() for k, v in carries[p].items()}
+            got = _np(ref.bot_act(leaves, p, bots[p][0], bots[p][1], ref_carry))
+            _diff(got, want, f"{where}: reference commands vs oracle")
+            for name, value in want_carry.items():
+                _diff(_np(ref_carry[name]), value, f"{where}: reference carry {name} vs oracle")
+            product_carry = _carry_to_gpu(carries[p], "cuda")
+            product = _np(gpu_bots[p].act(None, product_carry, state, env, p))
+            _diff(product, got, f"{where}: product commands vs reference")
+            _compare_carry(product_carry, {k: _np(v) for k, v in ref_carry.items()}, f"{where}: product carry vs reference")
+        want = orc.duel_step(tuple(b[0] for b in bots), tuple(b[1] for b in bots), carries)
+        ended += int(want["done"].sum())
+    torch.cuda.synchronize()
+    if config.startswith("c4"):
+        assert ended > 0, "no game ended inside the run"
+
+
+@pytest.mark.parametrize("config_name,lanes", [("c1_8x8_both", 48), ("c3_16x16_alternating_partial", 48)])
+def test_reference_timing_path_steps_like_the_oracle(config_name, lanes):
+    """The reference path bench.py times (the reference's kernels with torch
+    in place of its XLA fusions) steps games exactly as the oracle does,
+    auto-reset and masks included (configs without random conflict draws,
+    whose keys that path fixes)."""
+    ref_kernels = _reference()
+    from oracle.oracle import Oracle
+
+    cfg = CONFIGS[config_name]
+    game = cfg.game(100)
+    path = ref_kernels.ReferencePath(game, lanes, partial=cfg.partial)
+    orc = Oracle(game, lanes, partial_observability=cfg.partial)
+    orc.reset(np.zeros((lanes, 2), np.uint32))
+    rng = np.random.default_rng(3)
+    for t in range(250):
+        masks = orc.legal_masks()
+        actions = sample(masks, rng, 0.4)
+        rows = path.step(timed=False, actions=torch.from_numpy(actions).cuda())
+        _diff(_np(rows).astype(np.uint8), masks, f"{config_name} step {t}: masks")
+        orc.step(actions)
+        for name in LEAVES:
+            _diff(_np(path.leaves[name]), orc.state[name], f"{config_name} step {t}: leaf {name}")
