@@ -623,11 +623,14 @@ def measure_random(run: Run, config: int, lanes: int, steps: int, warmup: int, e
 
     # End to end through the public API with host buffers: each step copies the
     # actions from pinned host memory, steps (drawing the next actions on the
-    # device as the timed steps do) and reads the next actions, rewards and
-    # dones back to the host.  The rank's games run as E2E_SHARDS environment
-    # states, each on its own stream, so that one shard's host->device copy
-    # overlaps another's device->host copy (PCIe moves both ways at once).
-    # Pinned buffers sit on the GPU's NUMA node.
+    # device as the timed steps do) and writes the next actions, rewards and
+    # dones back to pinned host memory, where the next step's actions are read
+    # from.  The round trip is stream-ordered: no host synchronisation per step
+    # (the host reads the rewards and dones of every step, from a ring of
+    # per-step buffers, after the loop).  The rank's games run as E2E_SHARDS
+    # environment states, each on its own stream, so that one shard's
+    # host->device copy overlaps another's device->host copy and kernels (PCIe
+    # moves both ways at once).  Pinned buffers sit on the GPU's NUMA node.
     C = game.bucket.per_player_capacity
     # Small batches (under 32 MB of actions per step) stay one state: there the
     # per-launch latency outweighs the copy overlap.
@@ -645,8 +648,8 @@ def measure_random(run: Run, config: int, lanes: int, steps: int, warmup: int, e
                     "state": st,
                     "host": torch.empty((2, per, C, 7), dtype=torch.int32).pin_memory(),
                     "dev": torch.empty((2, per, C, 7), dtype=torch.int32, device=device),
-                    "rewards": torch.empty((per, 2), dtype=torch.float32).pin_memory(),
-                    "dones": torch.empty((per,), dtype=torch.bool).pin_memory(),
+                    "rewards": torch.empty((e2e_steps + 3, per, 2), dtype=torch.float32).pin_memory(),
+                    "dones": torch.empty((e2e_steps + 3, per), dtype=torch.bool).pin_memory(),
                 }
                 sh["host"][0].copy_(first["player_0"])
                 sh["host"][1].copy_(first["player_1"])
@@ -666,14 +669,15 @@ def measure_random(run: Run, config: int, lanes: int, steps: int, warmup: int, e
                     nxt = env.sample_actions(sh["state"], seed=rank, counter=2 * 10**9 + i)
                 sh["host"][0].copy_(nxt["player_0"], non_blocking=True)
                 sh["host"][1].copy_(nxt["player_1"], non_blocking=True)
-                sh["rewards"].copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
-                sh["dones"].copy_(dones["__all__"], non_blocking=True)
-        for s_k in streams:
-            s_k.synchronize()
+                sh["rewards"][i].copy_(torch.stack([rewards["player_0"], rewards["player_1"]], 1), non_blocking=True)
+                sh["dones"][i].copy_(dones["__all__"], non_blocking=True)
 
     stream = torch.cuda.current_stream(device)
+    e2e_steps_total = e2e_steps + 3
     for i in range(3):
         e2e_step(i)
+    for s_k in streams:
+        s_k.synchronize()
     run.barrier()
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -688,6 +692,7 @@ def measure_random(run: Run, config: int, lanes: int, steps: int, warmup: int, e
     torch.cuda.synchronize(device)
     (e2e_ms,) = run.max_over_ranks([e0.elapsed_time(e1)])
     run.check_device(f"the end-to-end steps of config {config}")
+    ended_e2e = sum(int(sh["dones"][:e2e_steps_total].sum()) for sh in shards)  # the host reads every step's results
 
     bytes_per = algorithmic_bytes(game, fused)
     h2d = global_games * C * 7 * 4 * 2
@@ -720,6 +725,8 @@ def measure_random(run: Run, config: int, lanes: int, steps: int, warmup: int, e
             "d2h_bytes_per_step": d2h,
             "shards_per_gpu": K,
             "host_copy_gbs": (h2d + d2h) * e2e_steps / (e2e_ms * 1e-3) / 1e9,
+            "loop": "stream-ordered host round trip of actions and results, no host synchronisation per step",
+            "games_ended": ended_e2e,
             "pinned_buffers": "on the GPU's NUMA node" if placement.cpus else "default placement (NVML affinity unknown)",
         },
         "gpu_launches": (1 if fused else 2) * steps,
