@@ -185,8 +185,8 @@ struct RowRef {
 };
 
 __device__ __forceinline__ bool bot_row(const Params& P, char* slab, int64_t game, int r, bool leaves, RowRef& out) {
-    if (r >= kSlabLeaves || !leaves) return false;
     const Layout& L = P.layout;
+    if (!staged_row<0>(r) || !leaves) return false;
     out.global = global_row(P, r, game);
     out.smem = slab_row(slab, L, r, out.global);
     out.bytes = static_cast<uint32_t>(L.row_bytes[r]);

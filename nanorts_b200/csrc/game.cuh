@@ -1,9 +1,9 @@
 // Kernel parameters, the per-game shared-memory slab and its staging.
 //
-// A game's State rows (the 14 per-slot leaves and entity_at, lane-major in
-// HBM) are copied into the owning warp's slab with 1D TMA bulk copies that
+// A game's State rows (the per-slot leaves and entity_at, lane-major in HBM)
+// are copied into the owning warp's slab with 1D TMA bulk copies that
 // complete on the warp's mbarrier, and written back in place with TMA bulk
-// stores.  A row's copy in the slab starts at its region plus the global
+// stores; on wide boards the rules-only pending rows stay in HBM (kRulesRows).  A row's copy in the slab starts at its region plus the global
 // address's offset within 16 bytes, so the row's 16-byte-aligned body maps
 // onto 16-byte-aligned shared memory; unaligned heads and tails (rows of
 // boards whose slot counts are not multiples of 16) are copied by the lanes.
@@ -29,6 +29,17 @@ constexpr int kMaxWidth = 64;
 constexpr int kMaxHeight = 64;
 constexpr int kMaxMaskBits = 96;
 constexpr int kSlabLeaves = 15;  // 14 per-slot leaves + entity_at
+// Rows only the rules touch (pending direction, none duration, target cell,
+// produced type, issued at, completes at, order).  On boards whose staged
+// game would not fit a small slab (wide boards, one game per CTA) the rules
+// read and write them in place in HBM (through L2, where the CTA's prefetch
+// put them): the slab shrinks by a quarter and one more game fits per SM
+// (64x64: 4 CTAs instead of 3, measured 15 % faster).  On small boards, where
+// a warp's serial rules phases dominate, staging them measured faster.
+constexpr uint32_t kRulesRows = (1u << NRTS_PENDING_DIRECTION) | (1u << NRTS_PENDING_NONE_DURATION) |
+                                (1u << NRTS_PENDING_TARGET_CELL) | (1u << NRTS_PENDING_PRODUCED_TYPE) |
+                                (1u << NRTS_PENDING_ISSUED_AT) | (1u << NRTS_PENDING_COMPLETES_AT) |
+                                (1u << NRTS_PENDING_ORDER);
 constexpr int32_t kNoCap = INT32_MAX;
 constexpr uint64_t kWaitNanoseconds = 2000000000ull;  // bound on any wait: 2 s
 
@@ -74,7 +85,8 @@ struct Layout {
     int32_t bot_off;     // bot scratch (BotLayout), aliasing the admission scratch
     int32_t bar_off;     // mbarrier
     int32_t aligned;     // every leaf base and row is 16-byte aligned: rows copy whole, one TMA copy per lane
-    int32_t total_bytes; // sum of row_bytes
+    int32_t total_bytes; // sum of the staged rows' row_bytes
+    uint32_t hbm_rows;   // rows the rules use in place in HBM (kRulesRows or 0); the others are staged
     int32_t slab_bytes;
     int32_t header_bytes;  // CTA-wide constants: terrain rows, attack windows, unit table
 };
@@ -219,6 +231,18 @@ struct Game {
 
 __device__ __forceinline__ int64_t leaf_row_bytes(const Params& P, int leaf) { return P.layout.row_bytes[leaf]; }
 
+// Whether State row `leaf` lives in the slab, for a launch whose rows kHbm
+// stay in HBM (a kernel template constant: every slab pointer then stays
+// known to the compiler as shared memory).
+template <uint32_t kHbm>
+__host__ __device__ __forceinline__ constexpr bool staged_row(int leaf) {
+    return leaf >= 0 && leaf < kSlabLeaves && !((kHbm >> leaf) & 1u);
+}
+
+__host__ __forceinline__ bool staged_row(const Layout& L, int leaf) {
+    return leaf >= 0 && leaf < kSlabLeaves && !((L.hbm_rows >> leaf) & 1u);
+}
+
 __device__ __forceinline__ char* slab_row(char* slab, const Layout& L, int leaf, const void* global) {
     return slab + L.leaf_off[leaf] + (reinterpret_cast<uintptr_t>(global) & 15u);
 }
@@ -227,9 +251,14 @@ __device__ __forceinline__ char* global_row(const Params& P, int leaf, int64_t g
     return static_cast<char*>(P.leaf[leaf]) + game * P.layout.row_bytes[leaf];
 }
 
+// A game's view: staged rows in the slab, rules-only rows in place in HBM.
+template <uint32_t kHbm = 0>
 __device__ __forceinline__ Game game_view(const Params& P, char* slab, int64_t game) {
     const Layout& L = P.layout;
-    auto row = [&](int leaf) { return slab_row(slab, L, leaf, global_row(P, leaf, game)); };
+    auto row = [&](int leaf) {
+        char* global = global_row(P, leaf, game);
+        return staged_row<kHbm>(leaf) ? slab_row(slab, L, leaf, global) : global;
+    };
     Game g;
     g.birth = reinterpret_cast<int32_t*>(row(NRTS_BIRTH));
     g.unit_type = reinterpret_cast<int8_t*>(row(NRTS_UNIT_TYPE));
@@ -383,6 +412,7 @@ __device__ __forceinline__ void prefetch_game(const Params& P, int64_t game, int
 }
 
 // Global rows -> slab; scalar leaves -> slab scalars.
+template <uint32_t kHbm = 0>
 __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t* bar, uint32_t parity, int lane,
                             bool scalars_at_once = false) {
     const Layout& L = P.layout;
@@ -395,19 +425,20 @@ __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t*
         const uintptr_t end = (base + (game + 1) * span) & ~uintptr_t{15};
         if (end > begin) bulk_prefetch_l2(reinterpret_cast<const void*>(begin), static_cast<uint32_t>(end - begin));
     }
+    const bool mine = staged_row<kHbm>(lane);
     if (L.aligned) {
         if (lane == 0) mbar_arrive_expect_tx(bar, static_cast<uint32_t>(L.total_bytes));
         __syncwarp();
-        if (lane < kSlabLeaves) bulk_load(slab + L.leaf_off[lane], global_row(P, lane, game), L.row_bytes[lane], bar);
+        if (mine) bulk_load(slab + L.leaf_off[lane], global_row(P, lane, game), L.row_bytes[lane], bar);
     } else {
         // Lane k owns row k: the TMA bulk copy of its 16-byte-aligned body and
         // its own unaligned head and tail bytes.
-        const char* src = lane < kSlabLeaves ? global_row(P, lane, game) : nullptr;
-        const Span sp = lane < kSlabLeaves ? split_row(src, L.row_bytes[lane]) : Span{0, 0, 0};
+        const char* src = mine ? global_row(P, lane, game) : nullptr;
+        const Span sp = mine ? split_row(src, L.row_bytes[lane]) : Span{0, 0, 0};
         const uint32_t total = __reduce_add_sync(kFull, sp.body);
         if (lane == 0) mbar_arrive_expect_tx(bar, total);
         __syncwarp();
-        if (lane < kSlabLeaves) {
+        if (mine) {
             char* dst = slab_row(slab, L, lane, src);
             if (sp.body) bulk_load(dst + sp.head, src + sp.head, sp.body, bar);
             copy_edge_in(dst, src, sp.head);
@@ -421,11 +452,14 @@ __device__ bool stage_state(const Params& P, char* slab, int64_t game, uint64_t*
     return ok;
 }
 
-// The reset State (one game's decided initial State, L2-resident) -> slab.
+// The reset State (one game's decided initial State, L2-resident) -> slab,
+// and its rules-only rows straight into the game's rows in HBM.
+template <uint32_t kHbm = 0>
 __device__ void load_reset(const Params& P, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     for (int k = 0; k < kSlabLeaves; ++k) {
-        char* dst = slab_row(slab, L, k, global_row(P, k, game));
+        char* global = global_row(P, k, game);
+        char* dst = staged_row<kHbm>(k) ? slab_row(slab, L, k, global) : global;
         const char* src = static_cast<const char*>(P.reset[k]);
         const int32_t bytes = L.row_bytes[k];
         if ((reinterpret_cast<uintptr_t>(dst) & 3u) == 0 && (bytes & 3) == 0) {
@@ -479,16 +513,17 @@ __device__ __forceinline__ void store_scalars(const Params& P, char* slab, int64
 
 // Slab -> global rows (TMA bulk stores of the bodies), scalars -> leaves.
 // Every lane that issued stores must later wait for its bulk group (finish_stores).
+template <uint32_t kHbm = 0>
 __device__ void store_state(const Params& P, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     fence_proxy_async_smem();
     __syncwarp();
     if (L.aligned) {
-        if (lane < kSlabLeaves) {
+        if (staged_row<kHbm>(lane)) {
             bulk_store(global_row(P, lane, game), slab + L.leaf_off[lane], L.row_bytes[lane]);
             bulk_commit();
         }
-    } else if (lane < kSlabLeaves) {  // lane k owns row k, as in stage_state
+    } else if (staged_row<kHbm>(lane)) {  // lane k owns row k, as in stage_state
         char* dst = global_row(P, lane, game);
         const Span sp = split_row(dst, L.row_bytes[lane]);
         const char* src = slab_row(slab, L, lane, dst);
@@ -501,8 +536,9 @@ __device__ void store_state(const Params& P, char* slab, int64_t game, int lane)
 }
 
 // Waits until the slab rows read by this lane's bulk stores may be reused.
+template <uint32_t kHbm = 0>
 __device__ __forceinline__ void finish_stores(const Params& P, int lane) {
-    if (lane < kSlabLeaves) bulk_wait_read_all();
+    if (staged_row<kHbm>(lane)) bulk_wait_read_all();
 }
 
 // The threads that write one game's outputs: its warp (tid = lane), or every

@@ -52,7 +52,7 @@ __device__ Header setup_header(const Params& P, char* smem) {
 // After admission: completion, outcome (outcome.py:11-37) and its outputs,
 // the optional observation of the ending state, and the lifecycle's auto-reset
 // (lifecycle.py:53-75).  Returns whether the game ended.
-template <int kW>
+template <int kW, uint32_t kHbm = 0>
 __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab,
                                                  int64_t game, int lane) {
     complete(P, H, G, g, slab, lane);
@@ -85,7 +85,7 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
         const int32_t episode = g.s[kSEpisode];
         const int32_t r0 = g.s[kSRoot0], r1 = g.s[kSRoot1];
         __syncwarp();
-        load_reset(P, slab, game, lane);
+        load_reset<kHbm>(P, slab, game, lane);
         if (lane == 0) {
             g.s[kSEpisode] = static_cast<int32_t>(static_cast<uint32_t>(episode) + 1u);
             g.s[kSRoot0] = r0;
@@ -98,27 +98,27 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
 
 // A game's State through the launch's mode, up to issuing its stores; false
 // when a bounded wait gave up.
-template <int kW>
+template <int kW, uint32_t kHbm = 0>
 __device__ __forceinline__ bool game_core(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
                                           uint32_t parity, int64_t game, int lane, bool team = false) {
-    Game g = game_view(P, slab, game);
+    Game g = game_view<kHbm>(P, slab, game);
     if (P.mode == kModeReset) {
-        load_reset(P, slab, game, lane);
+        load_reset<kHbm>(P, slab, game, lane);
         if (lane == 0) {
             g.s[kSEpisode] = 0;
             g.s[kSRoot0] = static_cast<int32_t>(P.keys[2 * game]);
             g.s[kSRoot1] = static_cast<int32_t>(P.keys[2 * game + 1]);
         }
         __syncwarp();
-    } else if (!stage_state(P, slab, game, bar, parity, lane, team)) {
+    } else if (!stage_state<kHbm>(P, slab, game, bar, parity, lane, team)) {
         return false;
     }
 
     if (P.mode == kModeStep) {
         admit(P, H, G, g, slab, game, lane);
-        finish_core_step(P, H, G, g, slab, game, lane);
+        finish_core_step<kW, kHbm>(P, H, G, g, slab, game, lane);
     }
-    if (P.mode != kModeOutputs) store_state(P, slab, game, lane);
+    if (P.mode != kModeOutputs) store_state<kHbm>(P, slab, game, lane);
     return true;
 }
 
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(32 * kBigWarps, 1) step_kernel_big(const __gri
 constexpr int kTeamWarps = 4;
 constexpr int32_t kWideSlabBytes = 24 * 1024;  // above this a game gets a CTA of its own
 
-template <int kW>
+template <int kW, uint32_t kHbm>
 __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __grid_constant__ Params P) {
     extern __shared__ __align__(128) char smem[];
     const int lane = threadIdx.x & 31;
@@ -212,16 +212,16 @@ __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __g
     for (int64_t g0 = blockIdx.x; g0 < P.lanes; g0 += gridDim.x) {
         const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
         if (warp == 0) {
-            const bool done = game_core(P, H, G, slab, bar, parity, game, lane, true);
+            const bool done = game_core<kW, kHbm>(P, H, G, slab, bar, parity, game, lane, true);
             if (lane == 0) *ok = done;
             const int64_t g1 = g0 + gridDim.x;
             if (done && P.mode == kModeStep && g1 < P.lanes) prefetch_game(P, P.reverse ? P.lanes - 1 - g1 : g1, lane);
         }
         __syncthreads();
         if (!*ok) break;
-        const Game g = game_view(P, slab, game);
+        const Game g = game_view<kHbm>(P, slab, game);
         write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, T);
-        if (warp == 0 && P.mode != kModeOutputs) finish_stores(P, lane);
+        if (warp == 0 && P.mode != kModeOutputs) finish_stores<kHbm>(P, lane);
         __syncthreads();
         if (P.mode != kModeReset) parity ^= 1u;
     }
@@ -476,8 +476,11 @@ int row_bytes_host(const NrtsExtents* x, int leaf) {
     }
 }
 
-Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
+// The slab layout of a launch; `hbm_rows` are rows the rules use in place
+// in HBM (no slab room), as the team kernel does on wide boards.
+Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots, uint32_t hbm_rows = 0u) {
     Layout L{};
+    L.hbm_rows = hbm_rows;
     const int E = x->neutral + 2 * x->capacity;
     const int owned = 2 * x->capacity;
     const int cells = x->height * x->width;
@@ -485,8 +488,8 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     int32_t off = 0;
     for (int k = 0; k < kSlabLeaves; ++k) {
         L.row_bytes[k] = row_bytes_host(x, k);
-        L.leaf_off[k] = off;
-        off += round16(L.row_bytes[k] + (aligned_rows ? 0 : 16));
+        L.leaf_off[k] = staged_row(L, k) ? off : -1;  // rows in HBM get no slab room
+        if (staged_row(L, k)) off += round16(L.row_bytes[k] + (aligned_rows ? 0 : 16));
     }
     L.scal_off = off;
     off += round16(kSCount * 4);
@@ -530,7 +533,8 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots) {
     L.slab_bytes = round16(off);
     L.aligned = aligned_rows ? 1 : 0;
     L.total_bytes = 0;
-    for (int k = 0; k < kSlabLeaves; ++k) L.total_bytes += L.row_bytes[k];
+    for (int k = 0; k < kSlabLeaves; ++k)
+        if (staged_row(L, k)) L.total_bytes += L.row_bytes[k];
     L.header_bytes = round16(sizeof(NrtsScenario));
     return L;
 }
@@ -543,14 +547,20 @@ struct DeviceInfo {
 
 DeviceInfo g_devices[64];
 
-const void* pick_wide_kernel(int width) {
+template <uint32_t kHbm>
+const void* pick_wide_kernel_rows(int width) {
     switch (width) {
-        case 8: return reinterpret_cast<const void*>(step_kernel_wide<8>);
-        case 16: return reinterpret_cast<const void*>(step_kernel_wide<16>);
-        case 32: return reinterpret_cast<const void*>(step_kernel_wide<32>);
-        case 64: return reinterpret_cast<const void*>(step_kernel_wide<64>);
-        default: return reinterpret_cast<const void*>(step_kernel_wide<0>);
+        case 8: return reinterpret_cast<const void*>(step_kernel_wide<8, kHbm>);
+        case 16: return reinterpret_cast<const void*>(step_kernel_wide<16, kHbm>);
+        case 32: return reinterpret_cast<const void*>(step_kernel_wide<32, kHbm>);
+        case 64: return reinterpret_cast<const void*>(step_kernel_wide<64, kHbm>);
+        default: return reinterpret_cast<const void*>(step_kernel_wide<0, kHbm>);
     }
+}
+
+// The team kernel of a board width, for a layout with or without rows in HBM.
+const void* pick_wide_kernel(int width, bool hbm = false) {
+    return hbm ? pick_wide_kernel_rows<kRulesRows>(width) : pick_wide_kernel_rows<0u>(width);
 }
 
 const void* pick_big_kernel(int width) {
@@ -606,8 +616,9 @@ int prepare_device(int& device, DeviceInfo*& info) {
             }
             if (cudaFuncSetAttribute(pick_groups_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(groups kernel) failed");
-            if (cudaFuncSetAttribute(pick_wide_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
-                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(wide kernel) failed");
+            for (bool hbm : {false, true})
+                if (cudaFuncSetAttribute(pick_wide_kernel(w, hbm), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                    return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(wide kernel) failed");
             if (cudaFuncSetAttribute(pick_big_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(big kernel) failed");
         }
@@ -662,6 +673,17 @@ int fill_params(Params& P, const NrtsExtents* x, const NrtsContent* content, con
     return NRTS_OK;
 }
 
+template <uint32_t kHbm>
+void launch_wide(const Params& P, unsigned blocks, int threads, size_t smem, cudaStream_t s) {
+    switch (P.width) {
+        case 8: step_kernel_wide<8, kHbm><<<blocks, threads, smem, s>>>(P); break;
+        case 16: step_kernel_wide<16, kHbm><<<blocks, threads, smem, s>>>(P); break;
+        case 32: step_kernel_wide<32, kHbm><<<blocks, threads, smem, s>>>(P); break;
+        case 64: step_kernel_wide<64, kHbm><<<blocks, threads, smem, s>>>(P); break;
+        default: step_kernel_wide<0, kHbm><<<blocks, threads, smem, s>>>(P); break;
+    }
+}
+
 template <int kW>
 void launch_instance(const Params& P, unsigned blocks, int threads, size_t smem, cudaStream_t stream) {
     if (P.mode == kModeDuel || P.mode == kModeBotAct) duel_kernel<kW><<<blocks, threads, smem, stream>>>(P);
@@ -703,12 +725,27 @@ int launch_step(Params& P, void* stream) {
         // of their games fit per SM anyway); smaller boards take the widest
         // team that keeps the whole batch resident at once, when the batch is
         // that small: their step is then bound by one game's latency.
-        const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
+        // Wide boards keep the rules-only rows in HBM (kRulesRows): a smaller
+        // slab, one more game per SM.
         const bool wide = L.slab_bytes > kWideSlabBytes;
+        if (wide) {
+            NrtsExtents x{};
+            x.height = P.height;
+            x.width = P.width;
+            x.neutral = P.neutral;
+            x.capacity = P.capacity;
+            x.types = P.types;
+            x.offsets = P.offsets;
+            x.strategy = P.strategy;
+            x.max_cycles = P.max_cycles;
+            x.partial_observability = P.partial;
+            P.layout = make_layout(&x, P.layout.aligned != 0, false, kRulesRows);
+        }
+        const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
         int team = 0, resident = 0;
         for (int warps = kTeamWarps; warps >= 2 && team == 0; warps /= 2) {
             int r = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, pick_wide_kernel(P.width), 32 * warps, smem) != cudaSuccess) r = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, pick_wide_kernel(P.width, wide), 32 * warps, smem) != cudaSuccess) r = 0;
             if (wide || static_cast<int64_t>(r) * info->sms >= P.lanes) {
                 team = warps;
                 resident = std::max(r, 1);
@@ -719,13 +756,8 @@ int launch_step(Params& P, void* stream) {
             const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(P.lanes, static_cast<int64_t>(info->sms) * resident));
             const int threads = 32 * team;
             cudaStream_t s = static_cast<cudaStream_t>(stream);
-            switch (P.width) {
-                case 8: step_kernel_wide<8><<<blocks, threads, smem, s>>>(P); break;
-                case 16: step_kernel_wide<16><<<blocks, threads, smem, s>>>(P); break;
-                case 32: step_kernel_wide<32><<<blocks, threads, smem, s>>>(P); break;
-                case 64: step_kernel_wide<64><<<blocks, threads, smem, s>>>(P); break;
-                default: step_kernel_wide<0><<<blocks, threads, smem, s>>>(P); break;
-            }
+            if (wide) launch_wide<kRulesRows>(P, blocks, threads, smem, s);
+            else launch_wide<0u>(P, blocks, threads, smem, s);
             const cudaError_t err = cudaGetLastError();
             if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("team kernel launch: ") + cudaGetErrorString(err));
             return NRTS_OK;
@@ -1093,7 +1125,9 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
                                  pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
                                  pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
                                  pick_groups_kernel(64), pick_groups_kernel(7), pick_wide_kernel(8), pick_wide_kernel(16),
-                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_big_kernel(8),
+                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_wide_kernel(8, true),
+                                 pick_wide_kernel(16, true), pick_wide_kernel(32, true), pick_wide_kernel(64, true),
+                                 pick_wide_kernel(7, true), pick_big_kernel(8),
                                  pick_big_kernel(16), pick_big_kernel(32), pick_big_kernel(64), pick_big_kernel(7),
                                  reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
                                  reinterpret_cast<const void*>(probe_kernel), reinterpret_cast<const void*>(wait_probe_kernel),
