@@ -361,7 +361,7 @@ def duel_cpu_baseline(game, seconds: float = 12.0, lanes: int = 256, threads: in
 # ---------------------------------------------------------------------------
 # The reference arm
 # ---------------------------------------------------------------------------
-def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int) -> dict:
+def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int, soak: int | None = None) -> dict:
     """The reference's own CUDA kernels (built unchanged for sm_100 by
     oracle/Makefile target `ref`) on this box's GPU, for the same workload:
     per step nanorts_legality_words, nanorts_visible_cells x2 (partial
@@ -376,7 +376,8 @@ def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int) -> d
         return {"unavailable": "oracle/_ref/libref_kernels.so not built (make -C oracle ref with a NanoRTS checkout)"}
     game = scenario(config)
     path = ref_kernels.ReferencePath(game, lanes, partial=CONFIGS[config][3], seed=0)
-    for _ in range(warmup + MIDPOINT[config]):  # mid-game states, as the timed steps of this implementation
+    soak = MIDPOINT[config] if soak is None else soak
+    for _ in range(warmup + soak):  # mid-game states, as the timed steps of this implementation
         path.step(timed=False)
     torch.cuda.synchronize()
     path.kernel_ms.clear()
@@ -392,7 +393,7 @@ def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int) -> d
         "kernel_ms_per_step": ms,
         "games": lanes,
         "steps": steps,
-        "untimed_steps_before": warmup + MIDPOINT[config],
+        "untimed_steps_before": warmup + soak,
         "kernels": kernels,
         "build": "reference sources unchanged, nvcc -O3 -gencode arch=compute_100,code=sm_100 (the image its own "
                  "build makes for a B200)",
@@ -465,7 +466,8 @@ def run_reference(args) -> None:
             import torch
 
             if torch.cuda.is_available():
-                line["gpu_kernels"] = reference_gpu_kernels(config, args.lanes, steps=min(args.steps, 50), warmup=3)
+                line["gpu_kernels"] = reference_gpu_kernels(config, args.lanes, steps=min(args.steps, 50), warmup=3,
+                                                            soak=args.soak_steps)
         except Exception as error:  # noqa: BLE001 - the CPU figure stands alone then
             line["gpu_kernels"] = {"unavailable": f"{type(error).__name__}: {error}"}
     print(json.dumps(line))
