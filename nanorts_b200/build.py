@@ -3,6 +3,8 @@
 ``python -m nanorts_b200.build`` or ``nanorts_b200.build.build()`` compiles
 ``csrc/*.cu`` into ``_lib/libnanorts_b200.so`` (cross-compiles without a GPU).
 The build is skipped when the library is newer than every source.
+``build_ffi()`` adds ``_lib/libnanorts_b200_ffi.so``, the jax.ffi handlers,
+where jaxlib's XLA FFI header is available.
 """
 
 from __future__ import annotations
@@ -50,5 +52,51 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return OUTPUT
 
 
+FFI_SOURCE = HERE / "ffi" / "nanorts_b200_ffi.cc"
+FFI_OUTPUT = HERE / "_lib" / "libnanorts_b200_ffi.so"
+
+
+def xla_ffi_include() -> Path | None:
+    """The directory holding jaxlib's ``xla/ffi/api/ffi.h``: ``XLA_FFI_INCLUDE``
+    when set, else ``jax.ffi.include_dir()`` when jax is importable, else None."""
+    named = os.environ.get("XLA_FFI_INCLUDE")
+    candidates = [Path(named)] if named else []
+    if not named:
+        try:
+            import jax.ffi  # noqa: PLC0415 - optional
+
+            candidates.append(Path(jax.ffi.include_dir()))
+        except Exception:  # noqa: BLE001 - jax absent or without ffi
+            pass
+    for root in candidates:
+        if (root / "xla" / "ffi" / "api" / "ffi.h").is_file():
+            return root
+    return None
+
+
+def build_ffi(force: bool = False, include: Path | None = None) -> Path | None:
+    """Compiles the jax.ffi handlers (ffi/nanorts_b200_ffi.cc) into
+    ``_lib/libnanorts_b200_ffi.so``, linked with the step library, where
+    jaxlib's XLA FFI header is found; returns None (and builds nothing) where
+    it is not."""
+    include = include or xla_ffi_include()
+    if include is None:
+        return None
+    library = build()
+    if not force and FFI_OUTPUT.exists() and FFI_OUTPUT.stat().st_mtime > max(
+            FFI_SOURCE.stat().st_mtime, library.stat().st_mtime, Path(__file__).stat().st_mtime):
+        return FFI_OUTPUT
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    cuda_include = Path(_nvcc()).resolve().parent.parent / "include"
+    tmp = FFI_OUTPUT.with_suffix(".so.tmp")
+    command = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", f"-I{include}", f"-I{HERE.parent / 'include'}",
+               f"-I{cuda_include}", "-o", str(tmp), str(FFI_SOURCE), f"-L{library.parent}", "-lnanorts_b200",
+               "-Wl,-rpath,$ORIGIN"]
+    subprocess.run(command, check=True)
+    tmp.replace(FFI_OUTPUT)
+    return FFI_OUTPUT
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_ffi(force="--force" in sys.argv) or "jax.ffi handlers skipped: no xla/ffi/api/ffi.h (jaxlib) found")

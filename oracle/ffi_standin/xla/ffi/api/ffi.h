@@ -3,7 +3,9 @@
 //
 // jaxlib is not installed here, so the reference's .cu files (core/cuda/step.cu,
 // core/cuda/legality.cu, observations/cuda/visibility.cu, adapters/cuda/reset.cu,
-// bots/cuda/abstraction_act.cu) cannot include the real header.  This file declares the types those files
+// bots/cuda/abstraction_act.cu) cannot include the real header; neither can
+// this repository's own XLA FFI handlers (nanorts_b200/ffi/nanorts_b200_ffi.cc),
+// which the tests build against this file to drive them without jaxlib.  This file declares the types those files
 // use -- buffers, errors, ErrorOr, the remaining-argument lists, the handler
 // macro -- with the same names and member functions, so the reference sources
 // compile unchanged.  XLA_FFI_DEFINE_HANDLER_SYMBOL does not register an XLA
@@ -206,6 +208,23 @@ class RemainingRets {
   private:
     const AnyBuffer* items_ = nullptr;
     size_t count_ = 0;
+};
+
+// A read-only array attribute.
+template <typename T>
+class Span {
+  public:
+    Span() = default;
+    Span(T* data, size_t size) : data_(data), size_(size) {}
+    T* data() const { return data_; }
+    size_t size() const { return size_; }
+    T& operator[](size_t k) const { return data_[k]; }
+    T* begin() const { return data_; }
+    T* end() const { return data_ + size_; }
+
+  private:
+    T* data_ = nullptr;
+    size_t size_ = 0;
 };
 
 template <typename T>
