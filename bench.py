@@ -374,6 +374,8 @@ def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int, soak
 
     if not ref_kernels.available():
         return {"unavailable": "oracle/_ref/libref_kernels.so not built (make -C oracle ref with a NanoRTS checkout)"}
+    if config == 4:
+        return reference_duel_kernels(lanes, steps, warmup, soak)
     game = scenario(config)
     path = ref_kernels.ReferencePath(game, lanes, partial=CONFIGS[config][3], seed=0)
     soak = MIDPOINT[config] if soak is None else soak
@@ -399,6 +401,39 @@ def reference_gpu_kernels(config: int, lanes: int, steps: int, warmup: int, soak
                  "build makes for a B200)",
         "excluded": "the reference's XLA fusions (action decode, observations, mask assembly, lifecycle select) "
                     "stand in as untimed torch ops; observations are not computed",
+    }
+
+
+def reference_duel_kernels(lanes: int, steps: int, warmup: int, soak: int | None = None) -> dict:
+    """Config 4 on the reference's own kernels (sm_100, same B200): per step
+    nanorts_abstraction_act for each player's bot, nanorts_step and
+    nanorts_reset_packed_where_done, with torch for the seat merge, the
+    counter select and the carry reset (untimed).  Kernel time only."""
+    import torch
+
+    from oracle import ref_kernels
+
+    path = ref_kernels.ReferenceDuelPath(scenario(4), lanes, DUEL_BOTS)
+    soak = MIDPOINT[4] if soak is None else soak
+    for _ in range(warmup + soak):
+        path.step(timed=False)
+    torch.cuda.synchronize()
+    path.kernel_ms.clear()
+    for _ in range(steps):
+        path.step(timed=True)
+    ms = statistics.mean(path.kernel_ms)
+    return {
+        "value": lanes / (ms * 1e-3),
+        "unit": "env-steps/s",
+        "kernel_ms_per_step": ms,
+        "games": lanes,
+        "steps": steps,
+        "untimed_steps_before": warmup + soak,
+        "kernels": ["nanorts_abstraction_act x2", "nanorts_step", "nanorts_reset_packed_where_done"],
+        "build": "reference sources unchanged, nvcc -O3 -gencode arch=compute_100,code=sm_100 (the image its own "
+                 "build makes for a B200)",
+        "excluded": "the seat merge of the two bots' Commands, the lifecycle select and the carry reset stand in as "
+                    "untimed torch ops",
     }
 
 
@@ -461,7 +496,7 @@ def run_reference(args) -> None:
                                    "runnable here (jax absent, reference install failed), so its C++ restatement runs"},
         "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    if config != 4 and not args.no_reference_kernels:
+    if not args.no_reference_kernels:
         try:
             import torch
 

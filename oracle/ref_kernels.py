@@ -362,3 +362,71 @@ class ReferencePath:
             torch.cuda.synchronize(self.device)
             self.kernel_ms.append(sum(a.elapsed_time(b) for a, b in marks))
         return rows
+
+
+class ReferenceDuelPath:
+    """The reference's CUDA path for config 4's bot-against-bot step on L
+    games: ``nanorts_abstraction_act`` for each player's rush bot (WorkerRush,
+    LightRush), ``nanorts_step`` on the two bots' Commands, and
+    ``nanorts_reset_packed_where_done``, with torch standing in for the JAX
+    between them (``seat_commands``' merge of each player's own rows,
+    bots/seat.py:152-157; the lifecycle's select of the counter leaves; the
+    empty carries of ended games, seat.py:127).  Only the reference kernels
+    are timed."""
+
+    def __init__(self, game: GameConfig, lanes: int, bots: tuple[tuple[int, int], tuple[int, int]],
+                 device: str | torch.device = "cuda") -> None:
+        from nanorts_b200.content import decide
+
+        self.ref = ReferenceKernels(game, device)
+        self.game, self.lanes, self.bots, self.device = game, lanes, bots, torch.device(device)
+        reset = decide(game.initial_state, game.bucket)
+        self.packed = self.ref.packed_reset_rows(reset)
+        self.reset_rows = {n: torch.from_numpy(np.ascontiguousarray(reset[n])).to(self.device) for n in LEAVES}
+        self.leaves = {n: v.expand(lanes, *v.shape).contiguous() for n, v in self.reset_rows.items()}
+        self.counters = {n: torch.empty_like(self.leaves[n]) for n in COUNTERS}
+        self.events = self.ref.event_buffers(lanes)
+        self.keys = torch.zeros((lanes, 2), dtype=torch.int32, device=self.device)  # CANCEL_BOTH draws nothing
+        C = game.bucket.per_player_capacity
+        self.carries = [self._empty_carry(lanes, C) for _ in range(2)]
+        self.kernel_ms: list[float] = []
+
+    def _empty_carry(self, lanes: int, capacity: int) -> dict[str, torch.Tensor]:
+        carry = {n: torch.full((lanes, capacity), -1, dtype=torch.int32, device=self.device) for n in CARRY_FIELDS}
+        carry["trained"] = torch.zeros((lanes, capacity), dtype=torch.uint8, device=self.device)
+        carry["next_order"] = torch.zeros((lanes,), dtype=torch.int32, device=self.device)
+        return carry
+
+    def step(self, timed: bool = True) -> torch.Tensor:
+        """One bot-against-bot step of every game; returns done bool [L]."""
+        stream = torch.cuda.current_stream(self.device)
+        marks = []
+
+        def run(call):
+            if timed:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                out = call()
+                b.record(stream)
+                marks.append((a, b))
+                return out
+            return call()
+
+        issued = [run(lambda p=p: self.ref.bot_act(self.leaves, p, self.bots[p][0], self.bots[p][1], self.carries[p]))
+                  for p in range(2)]
+        commands = [torch.cat([issued[0][:, f, :1], issued[1][:, f, 1:]], dim=1).contiguous() for f in range(6)]
+        run(lambda: self.ref.step(self.leaves, self.counters, commands, self.keys, self.events))
+        done = self.counters["game_over"] | (self.counters["time"] >= self.game.max_cycles)
+        run(lambda: self.ref.reset_where_done(done, self.packed, self.leaves))
+        for n in COUNTERS:
+            shape = (-1,) + (1,) * (self.counters[n].dim() - 1)
+            self.leaves[n].copy_(torch.where(done.view(shape), self.reset_rows[n], self.counters[n]))
+        for carry in self.carries:  # a finished game's carries start over from empty_actions
+            for n, v in carry.items():
+                fill = -1 if n in CARRY_FIELDS else 0
+                shape = (-1,) + (1,) * (v.dim() - 1)
+                v.copy_(torch.where(done.view(shape), torch.full_like(v, fill), v))
+        if timed:
+            torch.cuda.synchronize(self.device)
+            self.kernel_ms.append(sum(a.elapsed_time(b) for a, b in marks))
+        return done.reshape(-1)

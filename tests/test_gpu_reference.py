@@ -229,3 +229,35 @@ def test_reference_timing_path_steps_like_the_oracle(config_name, lanes):
         orc.step(actions)
         for name in LEAVES:
             _diff(_np(path.leaves[name]), orc.state[name], f"{config_name} step {t}: leaf {name}")
+
+
+def test_reference_duel_path_plays_like_the_oracle():
+    """The reference duel path bench.py times (the reference's bot, step and
+    reset kernels with torch for the seat merge, the counter select and the
+    carry reset) plays config 4 exactly as the oracle's duel step does,
+    through a game's end and restart."""
+    ref_kernels = _reference()
+    from nanorts_b200.model import ConflictStrategy, UnitTypeTableVersion
+    from oracle.oracle import Oracle, empty_carry
+    from tests.parity import Config
+
+    game = Config("c4", "basesWorkers16x16", UnitTypeTableVersion.ORIGINAL, ConflictStrategy.CANCEL_BOTH).game(5000)
+    bots = ((0, -1), (1, 4))
+    lanes = 4
+    path = ref_kernels.ReferenceDuelPath(game, lanes, bots)
+    orc = Oracle(game, lanes)
+    orc.reset(np.zeros((lanes, 2), np.uint32))
+    C = game.bucket.per_player_capacity
+    carries = (empty_carry(lanes, C), empty_carry(lanes, C))
+    ended = 0
+    for t in range(700):
+        want = orc.duel_step((bots[0][0], bots[1][0]), (bots[0][1], bots[1][1]), carries)
+        done = path.step(timed=False)
+        assert np.array_equal(_np(done), want["done"]), f"step {t}: done"
+        for name in LEAVES:
+            _diff(_np(path.leaves[name]), orc.state[name], f"step {t}: leaf {name}")
+        for p in range(2):
+            for name, value in carries[p].items():
+                _diff(_np(path.carries[p][name]), value, f"step {t}: carry {p} {name}")
+        ended += int(want["done"].sum())
+    assert ended > 0
