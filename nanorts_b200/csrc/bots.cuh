@@ -176,6 +176,11 @@ __device__ void store_carries(const Params& P, char* slab, int64_t game, int lan
     }
 }
 
+// Bot launches keep the rules-only rows in HBM (kRulesRows): their slab
+// shrinks from 15.5 KB to 12.6 KB per 16x16 game, 16 games fit per SM instead
+// of 14, and a bot-against-bot step measured 7 % faster.
+constexpr uint32_t kBotHbmRows = kRulesRows;
+
 // The State rows a bot launch moves between HBM and the slab (bot-act reads
 // the State and never writes it back).
 struct RowRef {
@@ -186,7 +191,7 @@ struct RowRef {
 
 __device__ __forceinline__ bool bot_row(const Params& P, char* slab, int64_t game, int r, bool leaves, RowRef& out) {
     const Layout& L = P.layout;
-    if (!staged_row<0>(r) || !leaves) return false;
+    if (!staged_row<kBotHbmRows>(r) || !leaves) return false;
     out.global = global_row(P, r, game);
     out.smem = slab_row(slab, L, r, out.global);
     out.bytes = static_cast<uint32_t>(L.row_bytes[r]);

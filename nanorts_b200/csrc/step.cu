@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(256, 3) groups_kernel(const __grid_constant__ 
 template <int kW>
 __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
                                          uint32_t parity, int64_t game, int lane) {
-    Game g = game_view(P, slab, game);
+    Game g = game_view<kBotHbmRows>(P, slab, game);
     if (!stage_bots(P, slab, game, bar, parity, lane)) return false;
     const bool duel = P.mode == kModeDuel;
     bot_prepare(P, H, G, g, slab, lane);
@@ -280,7 +280,7 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
         return true;
     }
     admit<kW, true>(P, H, G, g, slab, game, lane);
-    if (finish_core_step(P, H, G, g, slab, game, lane)) {
+    if (finish_core_step<kW, kBotHbmRows>(P, H, G, g, slab, game, lane)) {
         empty_carry(P, carry_view(P, slab, 0), lane);
         empty_carry(P, carry_view(P, slab, 1), lane);
     }
@@ -666,7 +666,7 @@ int fill_params(Params& P, const NrtsExtents* x, const NrtsContent* content, con
     P.root = state->environment_root;
     P.episode = state->episode_index;
     P.scenario = content->scenario;
-    P.layout = make_layout(x, aligned, bots);
+    P.layout = make_layout(x, aligned, bots, bots ? kBotHbmRows : 0u);
     int bits = 0;
     for (int v = x->capacity - 1; v > 0; v >>= 1) ++bits;
     P.rank_bits = bits > 1 ? bits : 1;  // admission.py:104-115
