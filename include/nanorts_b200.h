@@ -263,6 +263,28 @@ const char* nrts_build_id(void);
  * its own (the status word above is not touched).  Returns 0 when all pass. */
 int nrts_self_check(const int32_t* devices, int64_t count);
 
+/* The same checks as nrts_self_check, with no device allocation: no
+ * cudaMalloc, cudaFree or allocating library routine.  No counterpart in the
+ * reference (its self check, registry.cu:201-229, is nrts_self_check).
+ *
+ * For callers that cannot allocate device memory themselves.  A JAX process
+ * is the usual one: XLA's client takes most or all of each GPU's memory at
+ * start-up for its own allocator, so a cudaMalloc outside it can fail even
+ * for a few bytes, and a custom call is meant to draw memory only from XLA.
+ * nrts_self_check allocates 140 bytes per device for its probe results; this
+ * entry point writes them instead into a static device array of the library
+ * (64 int32, 256 bytes, present on every GPU that loads the library until the
+ * process exits).
+ *
+ * Limits: at most 64 devices per call, each index in 0..63; more, or a
+ * negative count, is refused with NRTS_E_ARGUMENT before any device work.
+ * The first call on a device looks up the array's device address with that
+ * device current (cudaGetSymbolAddress) and keeps it; make that first call
+ * before any stream capture.  Every call on a device reuses the same array
+ * (cleared at the start of each call), so calls that overlap on one GPU, from
+ * two host threads or processes sharing a context, race on it. */
+int nrts_self_check_no_alloc(const int32_t* devices, int64_t count);
+
 /* Message of the last failed call on this host thread. */
 const char* nrts_last_error(void);
 

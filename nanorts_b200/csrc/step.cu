@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/nanorts_b200.h"
@@ -420,6 +421,16 @@ __global__ void wait_probe_kernel(int32_t* out, uint64_t limit_ns) {
 // Reads and clears the status word in one atomic step.
 __device__ int32_t g_status_taken;
 __global__ void take_status_kernel() { g_status_taken = atomicExch(&g_status, 0); }
+
+// Probe words of nrts_self_check_no_alloc, in place of the buffer that
+// nrts_self_check allocates: words 0-32 take probe_kernel's results, words
+// 33-34 wait_probe_kernel's.  256 bytes on every device that loads the
+// library, held until the process exits; every call reuses them.
+constexpr int kNoAllocCheckWords = 64;
+constexpr int kNoAllocProbeWords = 33;
+constexpr int kNoAllocWaitWords = 2;
+static_assert(kNoAllocProbeWords + kNoAllocWaitWords <= kNoAllocCheckWords, "the probes' words fit the static array");
+static __device__ __align__(256) int32_t g_no_alloc_check[kNoAllocCheckWords];
 
 }  // namespace nrts
 
@@ -844,6 +855,45 @@ int check_bot(const NrtsExtents* x, const NrtsContent* content, const NrtsBot* b
     return NRTS_OK;
 }
 
+// Device addresses of g_no_alloc_check, one per device.  In host code the
+// array's name stands for a host-side shadow, never for device memory, so
+// the kernels get the address cudaGetSymbolAddress returns with the device
+// current: looked up on the first call that checks the device, kept after.
+int32_t* g_no_alloc_check_ptr[64] = {};
+std::mutex g_no_alloc_check_mutex;
+
+// The current device's copy of g_no_alloc_check (the caller made `device`
+// current).
+int no_alloc_check_words(int device, int32_t*& words) {
+    std::lock_guard<std::mutex> lock(g_no_alloc_check_mutex);
+    if (g_no_alloc_check_ptr[device] == nullptr) {
+        void* address = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&address, g_no_alloc_check);
+        if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("cudaGetSymbolAddress(probe words): ") + cudaGetErrorString(err));
+        g_no_alloc_check_ptr[device] = static_cast<int32_t*>(address);
+    }
+    words = g_no_alloc_check_ptr[device];
+    return NRTS_OK;
+}
+
+// Whether every kernel image of the library loads on the current device.
+bool kernel_images_load() {
+    const void* kernels[] = {pick_kernel(8), pick_kernel(16), pick_kernel(32), pick_kernel(64), pick_kernel(7),
+                             pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
+                             pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
+                             pick_groups_kernel(64), pick_groups_kernel(7), pick_wide_kernel(8), pick_wide_kernel(16),
+                             pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_wide_kernel(8, true),
+                             pick_wide_kernel(16, true), pick_wide_kernel(32, true), pick_wide_kernel(64, true),
+                             pick_wide_kernel(7, true), pick_big_kernel(8), pick_big_kernel(16), pick_big_kernel(32),
+                             pick_big_kernel(64), pick_big_kernel(7), reinterpret_cast<const void*>(sample_kernel),
+                             reinterpret_cast<const void*>(slot_cells_kernel), reinterpret_cast<const void*>(probe_kernel),
+                             reinterpret_cast<const void*>(wait_probe_kernel), reinterpret_cast<const void*>(take_status_kernel)};
+    cudaFuncAttributes attributes;
+    for (const void* k : kernels)
+        if (cudaFuncGetAttributes(&attributes, k) != cudaSuccess) return false;
+    return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1177,6 +1227,48 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
         if (probe[0] != 1 || probe[1] != 1) {
             cudaSetDevice(previous);
             return fail(NRTS_E_DEVICE, "a bounded wait did not give up and record its status");
+        }
+    }
+    cudaSetDevice(previous);
+    return NRTS_OK;
+}
+
+int nrts_self_check_no_alloc(const int32_t* devices, int64_t count) {
+    if (count < 0 || count > 64) return fail(NRTS_E_ARGUMENT, "the no-alloc self check takes between 0 and 64 devices per call");
+    if (count > 0 && devices == nullptr) return fail(NRTS_E_ARGUMENT, "devices is null");
+    for (int64_t i = 0; i < count; ++i)
+        if (devices[i] < 0 || devices[i] >= 64) return fail(NRTS_E_ARGUMENT, "a device index is outside 0..63");
+    int previous;
+    if (cudaGetDevice(&previous) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaGetDevice failed");
+    for (int64_t i = 0; i < count; ++i) {
+        const int device = devices[i];
+        int rc = NRTS_OK;
+        int32_t* words = nullptr;
+        cudaError_t err = cudaSetDevice(device);
+        if (err == cudaSuccess && !kernel_images_load()) rc = fail(NRTS_E_CUDA, "a kernel image does not load on this device");
+        if (err == cudaSuccess && rc == NRTS_OK) rc = no_alloc_check_words(device, words);
+        int32_t h[kNoAllocProbeWords + kNoAllocWaitWords] = {};
+        if (err == cudaSuccess && rc == NRTS_OK) {
+            // The words keep the previous call's results: clear them first,
+            // so that only this call's probes can set them.
+            err = cudaMemset(words, 0, kNoAllocCheckWords * sizeof(int32_t));
+            if (err == cudaSuccess) {
+                probe_kernel<<<1, 32>>>(words);
+                wait_probe_kernel<<<1, 32>>>(words + kNoAllocProbeWords, 1000000ull);
+                err = cudaGetLastError();
+            }
+            if (err == cudaSuccess) err = cudaMemcpy(h, words, sizeof(h), cudaMemcpyDeviceToHost);
+        }
+        if (err != cudaSuccess) rc = fail(NRTS_E_CUDA, cudaGetErrorString(err));
+        if (rc == NRTS_OK) {
+            for (int k = 0; k < kNoAllocProbeWords; ++k)
+                if (h[k] != 1) rc = fail(NRTS_E_DEVICE, "warp ballot or shuffle returned a wrong value");
+            if (rc == NRTS_OK && (h[kNoAllocProbeWords] != 1 || h[kNoAllocProbeWords + 1] != 1))
+                rc = fail(NRTS_E_DEVICE, "a bounded wait did not give up and record its status");
+        }
+        if (rc != NRTS_OK) {
+            cudaSetDevice(previous);
+            return rc;
         }
     }
     cudaSetDevice(previous);

@@ -85,7 +85,8 @@ class BotSpec(ctypes.Structure):
 SYMBOLS = (
     "nrts_prepare_scenario", "nrts_step", "nrts_step_groups", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
     "nrts_slot_cells", "nrts_sample_actions",
-    "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_last_error",
+    "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_build_id", "nrts_self_check", "nrts_self_check_no_alloc",
+    "nrts_last_error",
 )
 
 _LIB: ctypes.CDLL | None = None
@@ -116,11 +117,13 @@ def library() -> ctypes.CDLL:
     lib.nrts_duel_step.argtypes = [p, p, p, i64, p, p, p]
     lib.nrts_device_status.argtypes = [ctypes.c_int]
     lib.nrts_self_check.argtypes = [p, i64]
+    lib.nrts_self_check_no_alloc.argtypes = [p, i64]
     lib.nrts_build_id.restype = ctypes.c_char_p
     lib.nrts_last_error.restype = ctypes.c_char_p
     for name in ("nrts_prepare_scenario", "nrts_step", "nrts_step_groups", "nrts_reset", "nrts_legal_masks", "nrts_packed_masks", "nrts_observe",
                  "nrts_slot_cells",
-                 "nrts_sample_actions", "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_self_check"):
+                 "nrts_sample_actions", "nrts_bot_act", "nrts_duel_step", "nrts_device_status", "nrts_self_check",
+                 "nrts_self_check_no_alloc"):
         getattr(lib, name).restype = i32
     _LIB = lib
     return lib

@@ -166,6 +166,19 @@ def test_negative_lane_counts_are_refused(lib):
     assert "negative" in lib.nrts_last_error().decode()
 
 
+def test_no_alloc_self_check_refuses_device_lists_beyond_its_limits(lib):
+    """More than 64 devices, a negative count or an index outside 0..63 is
+    refused before any device work."""
+    devices = (ctypes.c_int32 * 65)(*([0] * 65))
+    assert lib.nrts_self_check_no_alloc(devices, 65) == -1
+    assert "64 devices" in lib.nrts_last_error().decode()
+    assert lib.nrts_self_check_no_alloc(devices, -1) == -1
+    assert lib.nrts_self_check_no_alloc(None, 1) == -1
+    assert "null" in lib.nrts_last_error().decode()
+    assert lib.nrts_self_check_no_alloc((ctypes.c_int32 * 1)(64), 1) == -1
+    assert "0..63" in lib.nrts_last_error().decode()
+
+
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(runtime, "LIBRARY", tmp_path / "absent.so")
     monkeypatch.setattr(runtime, "_LIB", None)
