@@ -66,7 +66,7 @@ KERNELS = {
     1: ("nrts::step_kernel_wide<8> (2-warp CTAs, the whole batch resident)", None),
     2: ("nrts::step_kernel_big<16>", "step_kernel_16x16_traffic.txt"),
     3: ("nrts::step_kernel_big<16>", "step_kernel_16x16_partial_traffic.txt"),
-    4: ("nrts::duel_kernel<16>", "duel_kernel_16x16_traffic.txt"),
+    4: ("nrts::duel_kernel_big<16>", "duel_kernel_16x16_traffic.txt"),
     5: ("nrts::step_kernel_wide<64>", "step_kernel_64x64_traffic.txt"),
 }
 

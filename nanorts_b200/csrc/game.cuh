@@ -64,7 +64,7 @@ struct Layout {
     int32_t list_off;    // int16 [2C]: requests, then members, then the available units
     int32_t order_off;   // int16 [2C]: sorted requests, then sorted members
     // Admission scratch.
-    int32_t serial_off;  // int16 [2C] ranks of the contested requests
+    int32_t serial_off;  // int16 [2C] ranks of the contested requests (over `count`, read by then)
     int32_t scan_off;    // int16 [E]:  claim holders scanned by contested requests
     int32_t conf_off;    // int16 [E]:  conflicting holders
     int32_t key_off;     // uint32 [2C] sort keys

@@ -512,6 +512,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
     }
     __syncwarp();
     if (lane == 0) g.s[kSNextOrder] = next_order + appended;
+    // `serial` lies over the claim counts: the loop above read them last.
     int16_t* serial = reinterpret_cast<int16_t*>(slab + L.serial_off);
     const int32_t S = warp_compact(R, lane, serial, [&](int32_t r) { return info[order[r]].serial != 0; });
     if (S > 0) admit_contested(P, H, G, g, slab, lane, S, holders);

@@ -295,8 +295,9 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
     return true;
 }
 
+// Each warp runs the bot launch's games block * warps + warp + k * (blocks * warps).
 template <int kW>
-__global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Params P) {
+__device__ __forceinline__ void duel_block(const Params& P) {
     extern __shared__ __align__(128) char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -318,6 +319,22 @@ __global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Param
         if (!run_bots(P, H, G, slab, bar, parity, game, lane)) break;
         parity ^= 1u;
     }
+}
+
+template <int kW>
+__global__ void __launch_bounds__(256) duel_kernel(const __grid_constant__ Params P) {
+    duel_block<kW>(P);
+}
+
+// Full bot batches: one CTA per SM holding up to kDuelBigWarps games, on a
+// persistent grid.  The bound of 20 warps per SM caps registers at 102 per
+// thread (the kernel needs 96), where the 8-warp CTAs of duel_kernel take
+// 128 and fit 16 games per SM.
+constexpr int kDuelBigWarps = 20;
+
+template <int kW>
+__global__ void __launch_bounds__(32 * kDuelBigWarps, 1) duel_kernel_big(const __grid_constant__ Params P) {
+    duel_block<kW>(P);
 }
 
 // Uniform draw per factor group from mask rows in HBM (nrts_sample_actions).
@@ -518,14 +535,16 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots, uint32_t 
     // outcome that reads its free-slot bitmaps) and the epilogue.  The
     // epilogue keeps only `list` (its available units) and starts at `order`.
     const int32_t U = off;
-    L.serial_off = U;
-    L.scan_off = L.serial_off + round16(owned * 2);
+    L.scan_off = U;
     L.conf_off = L.scan_off + round16(E * 2);
     L.key_off = L.conf_off + round16(E * 2);
     L.info_off = L.key_off + round16(owned * 4);
     L.rank_off = L.info_off + round16(owned * 12);
     L.count_off = L.rank_off + round16(owned * 2);
-    const int32_t end_admission = L.count_off + round16(((cells + 3) / 4) * 4 + 8 + 2 * 5 * 4);
+    // The contested requests' ranks are listed after the last read of the
+    // claim counts, into the same bytes.
+    L.serial_off = L.count_off;
+    const int32_t end_admission = L.count_off + std::max(round16(((cells + 3) / 4) * 4 + 8 + 2 * 5 * 4), round16(owned * 2));
     L.free_off = U;
     L.member_key_off = L.free_off + round16(2 * free_words * 4);
     L.ret_off = L.member_key_off + round16(owned * 4);
@@ -584,6 +603,16 @@ const void* pick_big_kernel(int width) {
     }
 }
 
+const void* pick_duel_big_kernel(int width) {
+    switch (width) {
+        case 8: return reinterpret_cast<const void*>(duel_kernel_big<8>);
+        case 16: return reinterpret_cast<const void*>(duel_kernel_big<16>);
+        case 32: return reinterpret_cast<const void*>(duel_kernel_big<32>);
+        case 64: return reinterpret_cast<const void*>(duel_kernel_big<64>);
+        default: return reinterpret_cast<const void*>(duel_kernel_big<0>);
+    }
+}
+
 const void* pick_groups_kernel(int width) {
     switch (width) {
         case 8: return reinterpret_cast<const void*>(groups_kernel<8>);
@@ -632,6 +661,8 @@ int prepare_device(int& device, DeviceInfo*& info) {
                     return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(wide kernel) failed");
             if (cudaFuncSetAttribute(pick_big_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
                 return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(big kernel) failed");
+            if (cudaFuncSetAttribute(pick_duel_big_kernel(w), cudaFuncAttributeMaxDynamicSharedMemorySize, info->smem_optin) != cudaSuccess)
+                return fail(NRTS_E_CUDA, "cudaFuncSetAttribute(duel big kernel) failed");
         }
         info->ready = true;
     }
@@ -699,6 +730,31 @@ template <int kW>
 void launch_instance(const Params& P, unsigned blocks, int threads, size_t smem, cudaStream_t stream) {
     if (P.mode == kModeDuel || P.mode == kModeBotAct) duel_kernel<kW><<<blocks, threads, smem, stream>>>(P);
     else step_kernel<kW><<<blocks, threads, smem, stream>>>(P);
+}
+
+template <int kW>
+void launch_big(const Params& P, unsigned grid, int threads, size_t smem, cudaStream_t stream) {
+    if (P.mode == kModeDuel || P.mode == kModeBotAct) duel_kernel_big<kW><<<grid, threads, smem, stream>>>(P);
+    else step_kernel_big<kW><<<grid, threads, smem, stream>>>(P);
+}
+
+// Games per SM of a one-CTA-per-SM step launch: each warp steps every
+// (SMs x warps)-th game, so the launch lasts as many rounds as its busiest
+// warp has games, and a round of more resident games takes longer (the SM's
+// issue slots are shared).  Of `top` and up to four fewer warps (more than
+// `floor`), the count with the fewest rounds x warps; the larger on a tie.
+int balanced_warps(int64_t lanes, int sms, int top, int floor) {
+    int best = top;
+    int64_t best_cost = INT64_MAX;
+    for (int w = top; w > floor && w >= top - 4; --w) {
+        const int64_t per_round = static_cast<int64_t>(sms) * w;
+        const int64_t cost = (lanes + per_round - 1) / per_round * w;
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = w;
+        }
+    }
+    return best;
 }
 
 // Warps per CTA with the most games resident per SM (registers and shared
@@ -787,23 +843,24 @@ int launch_step(Params& P, void* stream) {
             best_warps = warps;
         }
     }
-    if (!bots) {
+    {
         // One CTA per SM when that holds more games and the batch fills it.
         const int64_t room = (static_cast<int64_t>(info->smem_optin) - L.header_bytes) / L.slab_bytes;
-        const int big = static_cast<int>(std::min<int64_t>(kBigWarps, room));
+        int big = static_cast<int>(std::min<int64_t>(bots ? kDuelBigWarps : kBigWarps, room));
+        if (!bots) big = balanced_warps(P.lanes, info->sms, big, best_resident);
         int blocks = 0;
         const size_t smem = L.header_bytes + static_cast<size_t>(big) * L.slab_bytes;
+        const void* kernel_big = bots ? pick_duel_big_kernel(P.width) : pick_big_kernel(P.width);
         if (big > best_resident && P.lanes >= static_cast<int64_t>(info->sms) * big &&
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, pick_big_kernel(P.width), big * 32, smem) == cudaSuccess &&
-            blocks >= 1) {
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel_big, big * 32, smem) == cudaSuccess && blocks >= 1) {
             const unsigned grid = static_cast<unsigned>(info->sms);
             cudaStream_t s = static_cast<cudaStream_t>(stream);
             switch (P.width) {
-                case 8: step_kernel_big<8><<<grid, big * 32, smem, s>>>(P); break;
-                case 16: step_kernel_big<16><<<grid, big * 32, smem, s>>>(P); break;
-                case 32: step_kernel_big<32><<<grid, big * 32, smem, s>>>(P); break;
-                case 64: step_kernel_big<64><<<grid, big * 32, smem, s>>>(P); break;
-                default: step_kernel_big<0><<<grid, big * 32, smem, s>>>(P); break;
+                case 8: launch_big<8>(P, grid, big * 32, smem, s); break;
+                case 16: launch_big<16>(P, grid, big * 32, smem, s); break;
+                case 32: launch_big<32>(P, grid, big * 32, smem, s); break;
+                case 64: launch_big<64>(P, grid, big * 32, smem, s); break;
+                default: launch_big<0>(P, grid, big * 32, smem, s); break;
             }
             const cudaError_t err = cudaGetLastError();
             if (err != cudaSuccess) return fail(NRTS_E_CUDA, std::string("big kernel launch: ") + cudaGetErrorString(err));
@@ -885,7 +942,9 @@ bool kernel_images_load() {
                              pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_wide_kernel(8, true),
                              pick_wide_kernel(16, true), pick_wide_kernel(32, true), pick_wide_kernel(64, true),
                              pick_wide_kernel(7, true), pick_big_kernel(8), pick_big_kernel(16), pick_big_kernel(32),
-                             pick_big_kernel(64), pick_big_kernel(7), reinterpret_cast<const void*>(sample_kernel),
+                             pick_big_kernel(64), pick_big_kernel(7), pick_duel_big_kernel(8), pick_duel_big_kernel(16),
+                             pick_duel_big_kernel(32), pick_duel_big_kernel(64), pick_duel_big_kernel(7),
+                             reinterpret_cast<const void*>(sample_kernel),
                              reinterpret_cast<const void*>(slot_cells_kernel), reinterpret_cast<const void*>(probe_kernel),
                              reinterpret_cast<const void*>(wait_probe_kernel), reinterpret_cast<const void*>(take_status_kernel)};
     cudaFuncAttributes attributes;
@@ -1170,23 +1229,9 @@ int nrts_self_check(const int32_t* devices, int64_t count) {
     if (cudaGetDevice(&previous) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaGetDevice failed");
     for (int64_t i = 0; i < count; ++i) {
         if (cudaSetDevice(devices[i]) != cudaSuccess) return fail(NRTS_E_CUDA, "cudaSetDevice failed");
-        cudaFuncAttributes attributes;
-        const void* kernels[] = {pick_kernel(8), pick_kernel(16), pick_kernel(32), pick_kernel(64), pick_kernel(7),
-                                 pick_kernel(8, true), pick_kernel(16, true), pick_kernel(32, true), pick_kernel(64, true),
-                                 pick_kernel(7, true), pick_groups_kernel(8), pick_groups_kernel(16), pick_groups_kernel(32),
-                                 pick_groups_kernel(64), pick_groups_kernel(7), pick_wide_kernel(8), pick_wide_kernel(16),
-                                 pick_wide_kernel(32), pick_wide_kernel(64), pick_wide_kernel(7), pick_wide_kernel(8, true),
-                                 pick_wide_kernel(16, true), pick_wide_kernel(32, true), pick_wide_kernel(64, true),
-                                 pick_wide_kernel(7, true), pick_big_kernel(8),
-                                 pick_big_kernel(16), pick_big_kernel(32), pick_big_kernel(64), pick_big_kernel(7),
-                                 reinterpret_cast<const void*>(sample_kernel), reinterpret_cast<const void*>(slot_cells_kernel),
-                                 reinterpret_cast<const void*>(probe_kernel), reinterpret_cast<const void*>(wait_probe_kernel),
-                                 reinterpret_cast<const void*>(take_status_kernel)};
-        for (const void* k : kernels) {
-            if (cudaFuncGetAttributes(&attributes, k) != cudaSuccess) {
-                cudaSetDevice(previous);
-                return fail(NRTS_E_CUDA, "a kernel image does not load on this device");
-            }
+        if (!kernel_images_load()) {
+            cudaSetDevice(previous);
+            return fail(NRTS_E_CUDA, "a kernel image does not load on this device");
         }
         int32_t* d = nullptr;
         int32_t h[33];

@@ -174,6 +174,41 @@ def test_duel_matches_oracle(config):
     assert ended > 0, "no game ended inside the run"
 
 
+def test_duel_at_the_persistent_launch_shape_matches_oracle():
+    """Full batches run one CTA per SM holding up to 20 games, each warp
+    looping over every (SMs x warps)-th game: 6144 games on 148 SMs give
+    most warps two or three games per launch.  Short episodes (max_cycles
+    150) make games end and restart with empty carries inside the loop."""
+    from nanorts_b200.bots import Bot, Duel
+    from nanorts_b200.env import make
+    from oracle.oracle import empty_carry
+
+    game = BOT_CONFIGS["c4_16x16_both"].game(150)
+    bots = PAIRS["light_vs_worker"]
+    orc = _oracle_batch(game, [(2048, 0), (2048, 20), (2048, 60)], seed=11)
+    L, C = orc.lanes, game.bucket.per_player_capacity
+    assert L > 148 * 20
+    env = make("NanoRTS", scenario=game, final_observation=False)
+    duel = Duel(env, (Bot("p0", *bots[0]), Bot("p1", *bots[1])))
+    ds = duel.reset(torch.zeros((L, 2), dtype=torch.int32, device="cuda").view(torch.uint32))
+    _upload(ds.environment_state, orc)
+    carries = (empty_carry(L, C), empty_carry(L, C))
+    ended = 0
+    for step in range(200):
+        want = orc.duel_step(tuple(b[0] for b in bots), tuple(b[1] for b in bots), carries)
+        _, rewards, dones, infos = duel.step(ds)
+        torch.cuda.synchronize()
+        where = f"persistent duel step {step}"
+        _compare_state(ds.environment_state, orc, where)
+        for p in range(2):
+            _compare_carry(ds.carries[p], carries[p], f"{where} player {p}")
+        assert np.array_equal(_np(dones["__all__"]), want["done"]), f"{where}: done"
+        assert np.array_equal(_np(infos["winner"]), want["winner"]), f"{where}: winner"
+        ended += int(want["done"].sum())
+    assert ended >= L, f"only {ended} games ended"
+    print(f"persistent duel: {L} games, {ended} ended in 200 steps")
+
+
 def test_duel_outputs_observations_when_asked():
     """With observations on, the duel's masks and feature maps are those of the carried state."""
     from nanorts_b200.bots import Duel
