@@ -70,13 +70,13 @@ struct Layout {
     int32_t key_off;     // uint32 [2C] sort keys
     int32_t info_off;    // ReqInfo [2C]
     int32_t rank_off;    // int16 [2C] admission rank of each owned slot's request (-1 none)
-    int32_t count_off;   // uint8 [cells rounded to 4] claims per cell, 2 x uint32 produce claims, 2 x 5 int32 reward-component counts
+    int32_t count_off;   // uint32 [claim_words]: claims per cell (byte or 2-bit counters), 2 x uint32 produce claims, 2 x 5 int32 reward-component counts
     // Completion and outcome scratch (aliases admission scratch).
     int32_t free_off;    // uint32 [2 * ceil(C/32)]: free slots of each player block
     int32_t member_key_off;  // uint32 [2C] pending-order keys of the completing members
     int32_t ret_off;     // Retained [2C]
     // Epilogue scratch (aliases both, and `order` when no bots run).
-    int32_t word_off;    // uint32 [cells] occupant words
+    int32_t word_off;    // uint32 [cells] occupant words (per slot, [E], in slot-word layouts)
     int32_t rows_off;    // uint64 [4H] occupancy (2) and visibility (2) rows
     int32_t mask_off;    // uint32 [2C * 3 + 6] legality row words, then up to 4 per-warp counts
     // Scripted bots (duel and bot-act launches only; 0 otherwise).

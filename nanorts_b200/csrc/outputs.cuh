@@ -30,6 +30,65 @@ __device__ __forceinline__ uint32_t occupant_word(const Game& g, int32_t s) {
     return hp | (carried << 8) | (type << 16) | (pending << 24) | (owner << 28);
 }
 
+// Cell words kept in the slab, one per cell (built by cell_words).
+struct SlabWords {
+    const uint32_t* words;
+    __device__ __forceinline__ uint32_t at(int32_t c) const { return words[c]; }
+    // Cells c0 .. c0 + 7 (c0 a multiple of 8; two 16-byte loads).
+    __device__ __forceinline__ void eight(int32_t c0, uint32_t (&cw)[8]) const {
+        const uint4 qa = reinterpret_cast<const uint4*>(words + c0)[0];
+        const uint4 qb = reinterpret_cast<const uint4*>(words + c0)[1];
+        cw[0] = qa.x; cw[1] = qa.y; cw[2] = qa.z; cw[3] = qa.w;
+        cw[4] = qb.x; cw[5] = qb.y; cw[6] = qb.z; cw[7] = qb.w;
+    }
+};
+
+// Cell words gathered through entity_at from one occupant word per slot, as
+// the reference builds them (symbolic.py:149-168: word[clip(entity_at)] where
+// entity_at is not ABSENT), plus the wall bit: for slabs with no room for a
+// word per cell.
+template <int kW>
+struct SlotWords {
+    const Header& H;
+    const Geo<kW>& G;
+    const int16_t* entity_at;
+    const uint32_t* slot;  // occupant_word of every slot
+    int32_t entities;
+    __device__ __forceinline__ uint32_t occupant(int32_t s) const {
+        return s == kAbsent ? 0u : slot[clampi(s, 0, entities - 1)];
+    }
+    __device__ __forceinline__ uint32_t at(int32_t c) const {
+        const uint32_t wall = ((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u;
+        return occupant(entity_at[c]) | wall;
+    }
+    __device__ __forceinline__ void eight(int32_t c0, uint32_t (&cw)[8]) const {
+        int16_t at8[8];
+        if ((reinterpret_cast<uintptr_t>(entity_at + c0) & 15u) == 0) {
+            const uint4 q = *reinterpret_cast<const uint4*>(entity_at + c0);
+            const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                at8[2 * k] = static_cast<int16_t>(v[k] & 0xffffu);
+                at8[2 * k + 1] = static_cast<int16_t>(v[k] >> 16);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) at8[k] = entity_at[c0 + k];
+        }
+        if constexpr (kW >= 8) {  // eight cells of one row
+            const uint32_t walls = static_cast<uint32_t>(H.terrain_rows[G.y(c0)] >> G.x(c0)) & 0xffu;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) cw[k] = occupant(at8[k]) | (((walls >> k) & 1u) ? kWallBit : 0u);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int32_t c = c0 + k;
+                cw[k] = occupant(at8[k]) | (((H.terrain_rows[G.y(c)] >> G.x(c)) & 1ull) ? kWallBit : 0u);
+            }
+        }
+    }
+};
+
 // Disks of sight of each player's units (observations/visibility.py:70-77).
 template <int kW>
 __device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, uint64_t* vis, const Team& T) {
@@ -57,19 +116,19 @@ __device__ void visibility_rows(const Params& P, const Header& H, const Geo<kW>&
 }
 
 // Neighbour facts from occupant words (board.py:23-61 over board_view).
-template <int kW>
-__device__ __forceinline__ void neighbour_word(const Header& H, const Geo<kW>& G, const uint32_t* words, int32_t x, int32_t y, int d,
-                                               bool& free, uint32_t& word) {
+template <int kW, class Words>
+__device__ __forceinline__ void neighbour_word(const Geo<kW>& G, const Words& words, int32_t x, int32_t y, int d, bool& free,
+                                               uint32_t& word) {
     const int32_t nx = x + dir_dx(d), ny = y + dir_dy(d);
     const bool on_board = nx >= 0 && nx < G.width() && ny >= 0 && ny < G.h;
-    word = on_board ? words[ny * G.width() + nx] : kWallBit;
+    word = on_board ? words.at(ny * G.width() + nx) : kWallBit;
     free = word == 0u;
 }
 
 // Legality row of owned slot p as bits (legality.py:32-64, actions.py:28-41):
 // kind 6 | move 4 | harvest 4 | return 4 | produce direction 4 | produce type T | attack O.
-template <int kW>
-__device__ __forceinline__ void legality_row(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, const uint32_t* words,
+template <int kW, class Words>
+__device__ __forceinline__ void legality_row(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, const Words& words,
                                              const uint64_t* occ, uint32_t afford0, uint32_t afford1, int32_t p, uint32_t& w0, uint32_t& w1,
                                              uint32_t& w2) {
     const int32_t slot = P.neutral + p;
@@ -87,7 +146,7 @@ __device__ __forceinline__ void legality_row(const Params& P, const Header& H, c
     for (int d = 0; d < kDirections; ++d) {
         bool f;
         uint32_t w;
-        neighbour_word(H, G, words, cx, cy, d, f, w);
+        neighbour_word(G, words, cx, cy, d, f, w);
         const bool occupied = (w & kTypeField) != 0u;
         const int32_t t = clampi(static_cast<int32_t>((w >> 16) & 0xffu) - 1, 0, P.types - 1);
         const int32_t nowner = static_cast<int32_t>((w >> 28) & 0x3u) - 1;
@@ -211,8 +270,8 @@ __device__ __forceinline__ void features(uint32_t w, int player, bool shown, uin
     hi = ((w >> 24) & 0xfu) | (((w >> 30) & 1u) << 8);
 }
 
-template <int kW>
-__device__ void write_observation(const Params& P, const Geo<kW>& G, const Game& g, const uint32_t* words, const uint64_t* vis, int player,
+template <int kW, class Words>
+__device__ void write_observation(const Params& P, const Geo<kW>& G, const Game& g, const Words& words, const uint64_t* vis, int player,
                                   int64_t game, uint8_t* maps, int32_t* scalars, const Team& T) {
     if (maps != nullptr) {
         uint8_t* base = maps + game * static_cast<int64_t>(G.cells) * kFeatures;
@@ -226,12 +285,11 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
         };
         if ((G.cells & 7) == 0 && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
             // 8 cells = 48 bytes = three 16-byte stores; two cells fill three
-            // words.  The 8 cell words come in two 16-byte loads (lanes 32
-            // bytes apart: 2-way bank conflicts instead of 8-way for words).
+            // words.  The 8 cell words come by 16-byte loads (lanes 32 bytes
+            // apart: 2-way bank conflicts instead of 8-way for single words).
             for (int32_t c0 = T.tid * 8; c0 < G.cells; c0 += T.size * 8) {
-                const uint4 qa = reinterpret_cast<const uint4*>(words + c0)[0];
-                const uint4 qb = reinterpret_cast<const uint4*>(words + c0)[1];
-                const uint32_t cw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                uint32_t cw[8];
+                words.eight(c0, cw);
                 uint32_t w[12];
 #pragma unroll
                 for (int pair = 0; pair < 4; ++pair) {
@@ -250,7 +308,7 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
         } else {
             for (int32_t c = T.tid; c < G.cells; c += T.size) {
                 uint32_t lo, hi;
-                cell_features(c, words[c], lo, hi);
+                cell_features(c, words.at(c), lo, hi);
                 for (int b = 0; b < 4; ++b) base[c * kFeatures + b] = static_cast<uint8_t>(lo >> (8 * b));
                 base[c * kFeatures + 4] = static_cast<uint8_t>(hi);
                 base[c * kFeatures + 5] = static_cast<uint8_t>(hi >> 8);
@@ -345,6 +403,27 @@ __device__ __forceinline__ void cell_words(const Header& H, const Geo<kW>& G, co
     T.sync();
 }
 
+// One occupant word per slot (for SlotWords) and, when the masks need them,
+// the row bitmaps of the cells each player's active units occupy.
+template <int kW>
+__device__ __forceinline__ void slot_words(const Geo<kW>& G, const Game& g, uint32_t* slot, uint64_t* occ, bool rows, int32_t entities,
+                                           const Team& T) {
+    if (rows)
+        for (int32_t r = T.tid; r < 2 * G.h; r += T.size) occ[r] = 0ull;
+    T.sync();
+    for (int32_t s = T.tid; s < entities; s += T.size) {
+        const uint32_t w = occupant_word(g, s);
+        slot[s] = w;
+        if (!rows || g.birth[s] == kAbsent) continue;
+        const int32_t c = g.cell[s];
+        if (c < 0 || c >= G.cells || g.entity_at[c] != s) continue;
+        const uint32_t code = (w >> 28) & 3u;
+        if (code == 1u || code == 2u)
+            atomicOr(reinterpret_cast<unsigned long long*>(&occ[(code - 1) * G.h + G.y(c)]), 1ull << G.x(c));
+    }
+    T.sync();
+}
+
 // Zero int32 [count] at dst (4-byte aligned) with 16-byte stores where aligned.
 __device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, const Team& T) {
     const int32_t head = min(count, static_cast<int32_t>(((16u - (reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 2));
@@ -356,18 +435,14 @@ __device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, const Te
     if (T.tid < count - tail) dst[tail + T.tid] = 0;
 }
 
-template <int kW>
-__device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
-                              uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2], bool sample, const Team& T) {
+template <int kW, class Words>
+__device__ void write_outputs_from(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
+                                   const Words& words, uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2],
+                                   bool want_masks, bool want_obs, bool sample, const Team& T) {
     const Layout& L = P.layout;
-    uint32_t* words = reinterpret_cast<uint32_t*>(slab + L.word_off);
-    uint64_t* occ = reinterpret_cast<uint64_t*>(slab + L.rows_off);
-    uint64_t* vis = occ + 2 * G.h;
+    const uint64_t* occ = reinterpret_cast<const uint64_t*>(slab + L.rows_off);
+    uint64_t* vis = reinterpret_cast<uint64_t*>(slab + L.rows_off) + 2 * G.h;
     uint32_t* rows = reinterpret_cast<uint32_t*>(slab + L.mask_off);
-    const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample || P.out.packed_masks[0] != nullptr ||
-                            P.out.packed_masks[1] != nullptr;
-    const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
-    cell_words(H, G, g, words, occ, want_masks, P.entities, T);
     if (want_masks) {
         // Types each player can afford (the balance rule of produce.py:25-35).
         uint32_t afford0 = 0u, afford1 = 0u;
@@ -463,6 +538,28 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
             write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], T);
     }
     T.sync();
+}
+
+// A game's outputs from its slab.  kSlotWords: the layout holds one
+// occupant word per slot instead of one word per cell.
+template <int kW, bool kSlotWords = false>
+__device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
+                              uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2], bool sample, const Team& T) {
+    const Layout& L = P.layout;
+    uint64_t* occ = reinterpret_cast<uint64_t*>(slab + L.rows_off);
+    const bool want_masks = masks[0] != nullptr || masks[1] != nullptr || sample || P.out.packed_masks[0] != nullptr ||
+                            P.out.packed_masks[1] != nullptr;
+    const bool want_obs = maps[0] != nullptr || maps[1] != nullptr || scalars[0] != nullptr || scalars[1] != nullptr;
+    if constexpr (kSlotWords) {
+        uint32_t* slot = reinterpret_cast<uint32_t*>(slab + L.word_off);
+        slot_words(G, g, slot, occ, want_masks, P.entities, T);
+        const SlotWords<kW> words{H, G, g.entity_at, slot, P.entities};
+        write_outputs_from(P, H, G, g, slab, game, words, masks, maps, scalars, want_masks, want_obs, sample, T);
+    } else {
+        uint32_t* words = reinterpret_cast<uint32_t*>(slab + L.word_off);
+        cell_words(H, G, g, words, occ, want_masks, P.entities, T);
+        write_outputs_from(P, H, G, g, slab, game, SlabWords{words}, masks, maps, scalars, want_masks, want_obs, sample, T);
+    }
 }
 
 }  // namespace nrts

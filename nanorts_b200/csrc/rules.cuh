@@ -132,12 +132,32 @@ struct Retained {
 };
 static_assert(sizeof(Retained) == 20, "packed retained actor");
 
-__device__ __forceinline__ void add_claim(uint32_t* counts, int32_t cells, int32_t pos) {
-    if (pos >= 0 && pos < cells) atomicAdd(&counts[pos >> 2], 1u << (8 * (pos & 3)));
+// Claims per cell: a byte counter per cell, or (kTwoBit, for slabs short of
+// room) a 2-bit saturating counter, 16 cells per word, whose bit 0 the first
+// claim of a cell sets and bit 1 any later one.  Byte counters take one
+// atomic per claim and measured faster where the room is there.
+__host__ __device__ __forceinline__ int32_t claim_words(int32_t cells, bool two_bit) {
+    return two_bit ? (cells + 15) >> 4 : (cells + 3) >> 2;
 }
 
-__device__ __forceinline__ uint32_t claims_at(const uint32_t* counts, int32_t pos) {
-    return (counts[pos >> 2] >> (8 * (pos & 3))) & 0xffu;
+template <bool kTwoBit>
+__device__ __forceinline__ void add_claim(uint32_t* counts, int32_t cells, int32_t pos) {
+    if (pos < 0 || pos >= cells) return;
+    if constexpr (kTwoBit) {
+        const uint32_t shift = 2u * static_cast<uint32_t>(pos & 15);
+        const uint32_t before = atomicOr(&counts[pos >> 4], 1u << shift);
+        if ((before >> shift) & 1u) atomicOr(&counts[pos >> 4], 2u << shift);
+    } else {
+        atomicAdd(&counts[pos >> 2], 1u << (8 * (pos & 3)));
+    }
+}
+
+// Whether more than one claim names cell `pos`.
+template <bool kTwoBit>
+__device__ __forceinline__ bool claimed_twice(const uint32_t* counts, int32_t cells, int32_t pos) {
+    if (pos < 0 || pos >= cells) return false;
+    if constexpr (kTwoBit) return (counts[pos >> 4] >> (2u * static_cast<uint32_t>(pos & 15) + 1u)) & 1u;
+    else return ((counts[pos >> 2] >> (8 * (pos & 3))) & 0xffu) > 1u;
 }
 
 // Assigns a decided request's pending action (admission.py:241-270).
@@ -331,8 +351,9 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
 // player, rank, birth (admission.py:67-115); Commands hold, per player, either
 // no ranks or a permutation of ranks (model/commands.py:37-66), so the key
 // (player, rank) or (player, birth) orders them alike.  Bots issue commands
-// only to available units, the slots this pass scans.
-template <int kW, bool kCmd = false>
+// only to available units, the slots this pass scans.  kTwoBit: the
+// layout's claim counters are 2-bit (the compact layout of wide boards).
+template <int kW, bool kCmd = false, bool kTwoBit = false>
 __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     const int32_t N = P.neutral, C = P.capacity, E = P.entities;
@@ -344,7 +365,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
     ReqInfo* info = reinterpret_cast<ReqInfo*>(slab + L.info_off);
     int16_t* rank_of = reinterpret_cast<int16_t*>(slab + L.rank_off);
     uint32_t* counts = reinterpret_cast<uint32_t*>(slab + L.count_off);
-    const int32_t count_words = (G.cells + 3) >> 2;
+    const int32_t count_words = claim_words(G.cells, kTwoBit);
     uint32_t* produce_claims = counts + count_words;
 
     // Reward-component counts (admission.py:273-296 as adapters/rewards.py:47-72
@@ -370,7 +391,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         if (available) list[A + __popc(ma & lanes_below(lane))] = static_cast<int16_t>(s - N);
         if (holds) {
             scan[holders + __popc(mh & lanes_below(lane))] = static_cast<int16_t>(s);
-            add_claim(counts, G.cells, reserved_position(G, g.cell[s], g.pending_direction[s]));
+            add_claim<kTwoBit>(counts, G.cells, reserved_position(G, g.cell[s], g.pending_direction[s]));
             if (pk == kKindProduce) atomicAdd(&produce_claims[clampi(g.owner[s], 0, kPlayers - 1)], 1u);
         }
         if (in && s >= N) rank_of[s - N] = -1;
@@ -407,7 +428,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                         none = requested;
                     }
                 }
-                if (claims_kind(kind)) add_claim(counts, G.cells, pos);
+                if (claims_kind(kind)) add_claim<kTwoBit>(counts, G.cells, pos);
                 if (kind == kKindProduce) atomicAdd(&produce_claims[player], 1u);
                 if (counting) count_event(P, g, events + player * kEventCounts, player, kind, cptype, target);
                 ReqInfo r;
@@ -498,7 +519,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
             ReqInfo q = info[i];
             const int32_t player = (slot - N) >= C;
             const int32_t rcost = kind_cost(P, H, q.kind, q.ptype);
-            const bool contested = claims_kind(q.kind) && (claims_at(counts, q.pos) > 1 ||
+            const bool contested = claims_kind(q.kind) && (claimed_twice<kTwoBit>(counts, G.cells, q.pos) ||
                                                            (q.kind == kKindProduce && produce_claims[player] > 1));
             const bool serial = contested || (rcost > 0 && rcost > g.s[kSRes0 + player]);
             keys[i] = static_cast<uint32_t>(ord);

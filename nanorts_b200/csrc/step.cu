@@ -52,8 +52,9 @@ __device__ Header setup_header(const Params& P, char* smem) {
 
 // After admission: completion, outcome (outcome.py:11-37) and its outputs,
 // the optional observation of the ending state, and the lifecycle's auto-reset
-// (lifecycle.py:53-75).  Returns whether the game ended.
-template <int kW, uint32_t kHbm = 0>
+// (lifecycle.py:53-75).  Returns whether the game ended.  kCompact: the
+// compact layout (one occupant word per slot, 2-bit claim counters).
+template <int kW, uint32_t kHbm = 0, bool kCompact = false>
 __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab,
                                                  int64_t game, int lane) {
     complete(P, H, G, g, slab, lane);
@@ -80,7 +81,8 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
     }
     if (P.out.final_feature_maps[0] || P.out.final_feature_maps[1] || P.out.final_scalars[0] || P.out.final_scalars[1]) {
         uint8_t* const no_masks[2] = {nullptr, nullptr};
-        write_outputs(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false, warp_team(lane));
+        write_outputs<kW, kCompact>(P, H, G, g, slab, game, no_masks, P.out.final_feature_maps, P.out.final_scalars, false,
+                                      warp_team(lane));
     }
     if (done) {  // lifecycle.advance: the next episode starts from the reset State
         const int32_t episode = g.s[kSEpisode];
@@ -99,7 +101,7 @@ __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& 
 
 // A game's State through the launch's mode, up to issuing its stores; false
 // when a bounded wait gave up.
-template <int kW, uint32_t kHbm = 0>
+template <int kW, uint32_t kHbm = 0, bool kCompact = false>
 __device__ __forceinline__ bool game_core(const Params& P, const Header& H, const Geo<kW>& G, char* slab, uint64_t* bar,
                                           uint32_t parity, int64_t game, int lane, bool team = false) {
     Game g = game_view<kHbm>(P, slab, game);
@@ -116,8 +118,8 @@ __device__ __forceinline__ bool game_core(const Params& P, const Header& H, cons
     }
 
     if (P.mode == kModeStep) {
-        admit(P, H, G, g, slab, game, lane);
-        finish_core_step<kW, kHbm>(P, H, G, g, slab, game, lane);
+        admit<kW, false, kCompact>(P, H, G, g, slab, game, lane);
+        finish_core_step<kW, kHbm, kCompact>(P, H, G, g, slab, game, lane);
     }
     if (P.mode != kModeOutputs) store_state<kHbm>(P, slab, game, lane);
     return true;
@@ -188,12 +190,16 @@ __global__ void __launch_bounds__(32 * kBigWarps, 1) step_kernel_big(const __gri
 
 // Wide boards (a slab too large for more than a few games per SM): one game
 // per CTA of kTeamWarps warps.  Warp 0 runs the game's State through the
-// launch's mode; then every warp writes its outputs.
+// launch's mode; then every warp writes its outputs.  With the rules-only
+// rows in HBM (kHbm) the slab is also compact (one occupant word per slot
+// instead of one per cell, 2-bit claim counters): five games fit per SM on
+// 64 x 64 boards.
 constexpr int kTeamWarps = 4;
 constexpr int32_t kWideSlabBytes = 24 * 1024;  // above this a game gets a CTA of its own
 
 template <int kW, uint32_t kHbm>
-__global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(32 * kTeamWarps, kHbm ? 5 : 4) step_kernel_wide(const __grid_constant__ Params P) {
+    constexpr bool kCompact = kHbm != 0u;
     extern __shared__ __align__(128) char smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -213,7 +219,7 @@ __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __g
     for (int64_t g0 = blockIdx.x; g0 < P.lanes; g0 += gridDim.x) {
         const int64_t game = P.reverse ? P.lanes - 1 - g0 : g0;
         if (warp == 0) {
-            const bool done = game_core<kW, kHbm>(P, H, G, slab, bar, parity, game, lane, true);
+            const bool done = game_core<kW, kHbm, kCompact>(P, H, G, slab, bar, parity, game, lane, true);
             if (lane == 0) *ok = done;
             const int64_t g1 = g0 + gridDim.x;
             if (done && P.mode == kModeStep && g1 < P.lanes) prefetch_game(P, P.reverse ? P.lanes - 1 - g1 : g1, lane);
@@ -221,7 +227,8 @@ __global__ void __launch_bounds__(32 * kTeamWarps, 4) step_kernel_wide(const __g
         __syncthreads();
         if (!*ok) break;
         const Game g = game_view<kHbm>(P, slab, game);
-        write_outputs(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr, T);
+        write_outputs<kW, kCompact>(P, H, G, g, slab, game, P.out.masks, P.out.feature_maps, P.out.scalars, P.sampled[0] != nullptr,
+                                      T);
         if (warp == 0 && P.mode != kModeOutputs) finish_stores<kHbm>(P, lane);
         __syncthreads();
         if (P.mode != kModeReset) parity ^= 1u;
@@ -505,8 +512,10 @@ int row_bytes_host(const NrtsExtents* x, int leaf) {
 }
 
 // The slab layout of a launch; `hbm_rows` are rows the rules use in place
-// in HBM (no slab room), as the team kernel does on wide boards.
-Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots, uint32_t hbm_rows = 0u) {
+// in HBM (no slab room), as the team kernel does on wide boards, where its
+// layout is also `compact`: one occupant word per slot instead of one per
+// cell, 2-bit claim counters instead of byte counters.
+Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots, uint32_t hbm_rows = 0u, bool compact = false) {
     Layout L{};
     L.hbm_rows = hbm_rows;
     const int E = x->neutral + 2 * x->capacity;
@@ -544,13 +553,13 @@ Layout make_layout(const NrtsExtents* x, bool aligned_rows, bool bots, uint32_t 
     // The contested requests' ranks are listed after the last read of the
     // claim counts, into the same bytes.
     L.serial_off = L.count_off;
-    const int32_t end_admission = L.count_off + std::max(round16(((cells + 3) / 4) * 4 + 8 + 2 * 5 * 4), round16(owned * 2));
+    const int32_t end_admission = L.count_off + std::max(round16(claim_words(cells, compact) * 4 + 8 + 2 * 5 * 4), round16(owned * 2));
     L.free_off = U;
     L.member_key_off = L.free_off + round16(2 * free_words * 4);
     L.ret_off = L.member_key_off + round16(owned * 4);
     const int32_t end_completion = L.ret_off + round16(owned * 20);
     L.word_off = bots ? U : L.order_off;
-    L.rows_off = L.word_off + round16(cells * 4);
+    L.rows_off = L.word_off + round16((compact ? E : cells) * 4);
     L.mask_off = L.rows_off + round16(4 * x->height * 8);
     const int32_t end_epilogue = L.mask_off + round16((owned * 3 + 2 + 4) * 4);  // + the team counts
     off = std::max(end_admission, std::max(end_completion, end_epilogue));
@@ -792,8 +801,9 @@ int launch_step(Params& P, void* stream) {
         // of their games fit per SM anyway); smaller boards take the widest
         // team that keeps the whole batch resident at once, when the batch is
         // that small: their step is then bound by one game's latency.
-        // Wide boards keep the rules-only rows in HBM (kRulesRows): a smaller
-        // slab, one more game per SM.
+        // Wide boards keep the rules-only rows in HBM (kRulesRows) and a
+        // compact layout: a slab small enough for five games per SM on 64 x 64
+        // boards.
         const bool wide = L.slab_bytes > kWideSlabBytes;
         if (wide) {
             NrtsExtents x{};
@@ -806,7 +816,7 @@ int launch_step(Params& P, void* stream) {
             x.strategy = P.strategy;
             x.max_cycles = P.max_cycles;
             x.partial_observability = P.partial;
-            P.layout = make_layout(&x, P.layout.aligned != 0, false, kRulesRows);
+            P.layout = make_layout(&x, P.layout.aligned != 0, false, kRulesRows, true);
         }
         const size_t smem = L.header_bytes + static_cast<size_t>(L.slab_bytes);
         int team = 0, resident = 0;
