@@ -234,7 +234,9 @@ __device__ void write_masks(const Params& P, const uint32_t* rows, int64_t game,
         v.y = spread4((bits >> 4) & 0xfu);
         v.z = spread4((bits >> 8) & 0xfu);
         v.w = spread4((bits >> 12) & 0xfu);
-        *reinterpret_cast<uint4*>(base + head + 16 * k) = v;
+        // Evict-first (st.global.cs): the next launch reads the State and the
+        // drawn actions, not the masks, so they should not push those out of L2.
+        __stcs(reinterpret_cast<uint4*>(base + head + 16 * k), v);
         r += step_rows;
         c += step_cols;
         if (c >= width) {
@@ -300,10 +302,10 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
                     w[3 * pair + 1] = hi0 | (lo1 << 16);
                     w[3 * pair + 2] = (lo1 >> 16) | (hi1 << 16);
                 }
-                uint4* dst = reinterpret_cast<uint4*>(base + c0 * kFeatures);
-                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-                dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+                uint4* dst = reinterpret_cast<uint4*>(base + c0 * kFeatures);  // evict-first, as the masks
+                __stcs(dst, make_uint4(w[0], w[1], w[2], w[3]));
+                __stcs(dst + 1, make_uint4(w[4], w[5], w[6], w[7]));
+                __stcs(dst + 2, make_uint4(w[8], w[9], w[10], w[11]));
             }
         } else {
             for (int32_t c = T.tid; c < G.cells; c += T.size) {
