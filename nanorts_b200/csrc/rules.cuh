@@ -353,7 +353,9 @@ __device__ __forceinline__ void admit_contested(const Params& P, const Header& H
 // (player, rank) or (player, birth) orders them alike.  Bots issue commands
 // only to available units, the slots this pass scans.  kTwoBit: the
 // layout's claim counters are 2-bit (the compact layout of wide boards).
-template <int kW, bool kCmd = false, bool kTwoBit = false>
+// kHbmRows: the rules-only rows stay in HBM, so the holders' directions are
+// read after the pass, one load per holder at once, instead of inside it.
+template <int kW, bool kCmd = false, bool kTwoBit = false, bool kHbmRows = false>
 __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab, int64_t game, int lane) {
     const Layout& L = P.layout;
     const int32_t N = P.neutral, C = P.capacity, E = P.entities;
@@ -377,8 +379,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         reinterpret_cast<uint4*>(counts)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncwarp();
     // One pass over the slots: available owned slots (actions.py:65-75,
-    // legality.py:169-170) and the claim holders at the step's start, with
-    // their claimed cells counted.
+    // legality.py:169-170) and the claim holders at the step's start.
     int32_t A = 0, holders = 0;
     for (int32_t base = 0; base < E; base += 32) {
         const int32_t s = base + lane;
@@ -391,7 +392,7 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         if (available) list[A + __popc(ma & lanes_below(lane))] = static_cast<int16_t>(s - N);
         if (holds) {
             scan[holders + __popc(mh & lanes_below(lane))] = static_cast<int16_t>(s);
-            add_claim<kTwoBit>(counts, G.cells, reserved_position(G, g.cell[s], g.pending_direction[s]));
+            if constexpr (!kHbmRows) add_claim<kTwoBit>(counts, G.cells, reserved_position(G, g.cell[s], g.pending_direction[s]));
             if (pk == kKindProduce) atomicAdd(&produce_claims[clampi(g.owner[s], 0, kPlayers - 1)], 1u);
         }
         if (in && s >= N) rank_of[s - N] = -1;
@@ -399,6 +400,13 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
         holders += __popc(mh);
     }
     __syncwarp();
+    if constexpr (kHbmRows) {  // the holders' claimed cells, from the list
+        for (int32_t j = lane; j < holders; j += 32) {
+            const int32_t s = scan[j];
+            add_claim<kTwoBit>(counts, G.cells, reserved_position(G, g.cell[s], g.pending_direction[s]));
+        }
+        __syncwarp();
+    }
     // Decode every available slot's row (actions.py:61-84) and decide the issued
     // ones in parallel; a row whose kind is absent issues nothing.
     int32_t R = 0;
@@ -456,7 +464,9 @@ __device__ void admit(const Params& P, const Header& H, const Geo<kW>& G, Game& 
                 }
             } else {
                 const int32_t* row = P.actions[player] + (game * C + local) * kActionColumns;
-                const int32_t raw = row[0], r1 = row[1], r2 = row[2], r3 = row[3], r4 = row[4], r5 = row[5], r6 = row[6];
+                // Read once per step: evict-first loads (ld.global.cs).
+                const int32_t raw = __ldcs(row), r1 = __ldcs(row + 1), r2 = __ldcs(row + 2), r3 = __ldcs(row + 3),
+                              r4 = __ldcs(row + 4), r5 = __ldcs(row + 5), r6 = __ldcs(row + 6);
                 issued = raw != kAbsent;
                 if (issued) {
                     const int32_t raw_dir = raw == kKindMove ? r1 : raw == kKindHarvest ? r2 : raw == kKindReturn ? r3
@@ -553,7 +563,9 @@ __device__ __forceinline__ void free_set(uint32_t* free_words, const Params& P, 
     *w = is_free ? (*w | bit) : (*w & ~bit);
 }
 
-template <int kW>
+// kHbmRows: the rules-only rows stay in HBM; the pass reads them for the
+// pending slots only, listed first.
+template <int kW, bool kHbmRows = false>
 __device__ void complete(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab, int lane) {
     const Layout& L = P.layout;
     const int32_t N = P.neutral, E = P.entities, C = P.capacity;
@@ -565,13 +577,24 @@ __device__ void complete(const Params& P, const Header& H, const Geo<kW>& G, Gam
     const int32_t time = static_cast<int32_t>(static_cast<uint32_t>(g.s[kSTime]) + 1u);  // pending.select
     __syncwarp();
     if (lane == 0) g.s[kSTime] = time;
-    // One pass over the slots: the acting owned members (completed, kind !=
-    // NONE) listed with their retained facts, and every completed slot's
-    // pending action cleared (pending.clear).
+    // The acting owned members (completed, kind != NONE) listed with their
+    // retained facts, and every completed slot's pending action cleared
+    // (pending.clear): one pass over the slots, or with kHbmRows the neutral
+    // slots first and then the pending owned slots, listed in slot order from
+    // pending_kind alone (`order` is free until the ranking below), so that
+    // the rows in HBM are read for those slots only, with their loads at once.
+    int32_t Q = E;
+    if constexpr (kHbmRows) {
+        for (int32_t s = lane; s < N; s += 32) {
+            if (g.pending_kind[s] != kAbsent && g.pending_completes_at[s] <= time) g.clear_pending(s);
+        }
+        Q = warp_compact(P.owned, lane, order, [&](int32_t p) { return g.pending_kind[N + p] != kAbsent; });
+    }
     int32_t M = 0;
-    for (int32_t base = 0; base < E; base += 32) {
-        const int32_t s = base + lane;
-        const int32_t pk = s < E ? g.pending_kind[s] : kAbsent;
+    for (int32_t base = 0; base < Q; base += 32) {
+        int32_t s = base + lane;
+        if constexpr (kHbmRows) s = s < Q ? N + order[s] : 0;
+        const int32_t pk = base + lane < Q ? g.pending_kind[s] : kAbsent;
         const bool completed = pk != kAbsent && g.pending_completes_at[s] <= time;
         const bool acting = completed && pk != kKindNone && s >= N;
         const unsigned m = __ballot_sync(kFull, acting);

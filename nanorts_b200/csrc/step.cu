@@ -57,7 +57,7 @@ __device__ Header setup_header(const Params& P, char* smem) {
 template <int kW, uint32_t kHbm = 0, bool kCompact = false>
 __device__ __forceinline__ bool finish_core_step(const Params& P, const Header& H, const Geo<kW>& G, Game& g, char* slab,
                                                  int64_t game, int lane) {
-    complete(P, H, G, g, slab, lane);
+    complete<kW, (kHbm != 0u)>(P, H, G, g, slab, lane);
     bool terminated, truncated;
     decide(P, g, slab, lane, terminated, truncated);
     const bool done = terminated || truncated;
@@ -118,7 +118,7 @@ __device__ __forceinline__ bool game_core(const Params& P, const Header& H, cons
     }
 
     if (P.mode == kModeStep) {
-        admit<kW, false, kCompact>(P, H, G, g, slab, game, lane);
+        admit<kW, false, kCompact, (kHbm != 0u)>(P, H, G, g, slab, game, lane);
         finish_core_step<kW, kHbm, kCompact>(P, H, G, g, slab, game, lane);
     }
     if (P.mode != kModeOutputs) store_state<kHbm>(P, slab, game, lane);
@@ -287,7 +287,7 @@ __device__ __forceinline__ bool run_bots(const Params& P, const Header& H, const
         __syncwarp();
         return true;
     }
-    admit<kW, true>(P, H, G, g, slab, game, lane);
+    admit<kW, true, false, true>(P, H, G, g, slab, game, lane);
     if (finish_core_step<kW, kBotHbmRows>(P, H, G, g, slab, game, lane)) {
         empty_carry(P, carry_view(P, slab, 0), lane);
         empty_carry(P, carry_view(P, slab, 1), lane);
