@@ -323,6 +323,64 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
     }
 }
 
+// Both players' feature maps (and scalars) from one read of each group of 8
+// cells' words and visibility bits, on boards whose rows hold whole groups;
+// elsewhere one player at a time (write_observation).  For gathered words
+// (SlotWords): reading them once per group for both players measured 5 %
+// faster on config 5; with the slab's cell words (two 16-byte loads per group)
+// the per-player loops measured faster (config 2: 0.157 against 0.161 ms).
+template <int kW, class Words>
+__device__ void write_observations(const Params& P, const Geo<kW>& G, const Game& g, const Words& words, const uint64_t* vis,
+                                   int64_t game, uint8_t* const maps[2], int32_t* const scalars[2], const Team& T) {
+    uint8_t* base[2] = {nullptr, nullptr};
+    bool grouped = kW >= 8 && (kW & 7) == 0 && maps[0] != nullptr && maps[1] != nullptr;
+    for (int player = 0; player < kPlayers && grouped; ++player) {
+        base[player] = maps[player] + game * static_cast<int64_t>(G.cells) * kFeatures;
+        grouped = (reinterpret_cast<uintptr_t>(base[player]) & 15u) == 0;
+    }
+    if (!grouped) {
+        for (int player = 0; player < kPlayers; ++player)
+            write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], T);
+        return;
+    }
+    for (int32_t c0 = T.tid * 8; c0 < G.cells; c0 += T.size * 8) {
+        uint32_t cw[8];
+        words.eight(c0, cw);
+        uint32_t seen[2] = {0xffu, 0xffu};  // bit k: cell c0 + k visible to the player
+        if (P.partial) {
+            seen[0] = static_cast<uint32_t>(vis[G.y(c0)] >> G.x(c0)) & 0xffu;
+            seen[1] = static_cast<uint32_t>(vis[G.h + G.y(c0)] >> G.x(c0)) & 0xffu;
+        }
+#pragma unroll
+        for (int player = 0; player < kPlayers; ++player) {
+            uint32_t w[12];
+#pragma unroll
+            for (int pair = 0; pair < 4; ++pair) {
+                uint32_t lo[2], hi[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int k = 2 * pair + h;
+                    const bool shown = !P.partial || ((cw[k] >> 28) & 0x3u) == static_cast<uint32_t>(player + 1) || ((seen[player] >> k) & 1u);
+                    features(cw[k], player, shown, lo[h], hi[h]);
+                }
+                w[3 * pair] = lo[0];
+                w[3 * pair + 1] = hi[0] | (lo[1] << 16);
+                w[3 * pair + 2] = (lo[1] >> 16) | (hi[1] << 16);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(base[player] + c0 * kFeatures);  // evict-first, as the masks
+            __stcs(dst, make_uint4(w[0], w[1], w[2], w[3]));
+            __stcs(dst + 1, make_uint4(w[4], w[5], w[6], w[7]));
+            __stcs(dst + 2, make_uint4(w[8], w[9], w[10], w[11]));
+        }
+    }
+    for (int player = 0; player < kPlayers; ++player) {
+        if (scalars[player] != nullptr && T.tid == 0) {  // symbolic.py:171-180
+            *reinterpret_cast<int4*>(scalars[player] + game * kScalars) =
+                make_int4(g.s[kSRes0 + player], g.s[kSRes0 + 1 - player], g.s[kSTime], g.s[kSAlt]);
+        }
+    }
+}
+
 // Per-launch draw key from the caller's (seed, counter); host and device agree.
 __host__ __device__ __forceinline__ uint32_t sample_key(uint64_t seed, uint64_t counter) {
     uint32_t k = mix32(static_cast<uint32_t>(seed) ^ 0x9e3779b9u);
@@ -437,7 +495,7 @@ __device__ __forceinline__ void zero_words(int32_t* dst, int32_t count, const Te
     if (T.tid < count - tail) dst[tail + T.tid] = 0;
 }
 
-template <int kW, class Words>
+template <int kW, class Words, bool kGrouped = false>
 __device__ void write_outputs_from(const Params& P, const Header& H, const Geo<kW>& G, const Game& g, char* slab, int64_t game,
                                    const Words& words, uint8_t* const masks[2], uint8_t* const maps[2], int32_t* const scalars[2],
                                    bool want_masks, bool want_obs, bool sample, const Team& T) {
@@ -536,8 +594,12 @@ __device__ void write_outputs_from(const Params& P, const Header& H, const Geo<k
     }
     if (want_obs) {
         if (P.partial) visibility_rows(P, H, G, g, vis, T);
-        for (int player = 0; player < kPlayers; ++player)
-            write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], T);
+        if constexpr (kGrouped) {
+            write_observations(P, G, g, words, vis, game, maps, scalars, T);
+        } else {
+            for (int player = 0; player < kPlayers; ++player)
+                write_observation(P, G, g, words, vis, player, game, maps[player], scalars[player], T);
+        }
     }
     T.sync();
 }
@@ -556,7 +618,8 @@ __device__ void write_outputs(const Params& P, const Header& H, const Geo<kW>& G
         uint32_t* slot = reinterpret_cast<uint32_t*>(slab + L.word_off);
         slot_words(G, g, slot, occ, want_masks, P.entities, T);
         const SlotWords<kW> words{H, G, g.entity_at, slot, P.entities};
-        write_outputs_from(P, H, G, g, slab, game, words, masks, maps, scalars, want_masks, want_obs, sample, T);
+        write_outputs_from<kW, SlotWords<kW>, true>(P, H, G, g, slab, game, words, masks, maps, scalars, want_masks, want_obs, sample,
+                                                    T);
     } else {
         uint32_t* words = reinterpret_cast<uint32_t*>(slab + L.word_off);
         cell_words(H, G, g, words, occ, want_masks, P.entities, T);
