@@ -292,12 +292,29 @@ __device__ void write_observation(const Params& P, const Geo<kW>& G, const Game&
             for (int32_t c0 = T.tid * 8; c0 < G.cells; c0 += T.size * 8) {
                 uint32_t cw[8];
                 words.eight(c0, cw);
+                // Bit k: cell c0 + k visible to the player (one row load when
+                // the 8 cells share a row).
+                uint32_t seen = 0xffu;
+                if (P.partial) {
+                    if constexpr (kW >= 8 && (kW & 7) == 0) {
+                        seen = static_cast<uint32_t>(vis[player * G.h + G.y(c0)] >> G.x(c0)) & 0xffu;
+                    } else {
+                        seen = 0u;
+#pragma unroll
+                        for (int k = 0; k < 8; ++k)
+                            seen |= static_cast<uint32_t>((vis[player * G.h + G.y(c0 + k)] >> G.x(c0 + k)) & 1ull) << k;
+                    }
+                }
+                auto group_features = [&](int k, uint32_t& lo, uint32_t& hi) {
+                    const bool shown = !P.partial || ((cw[k] >> 28) & 0x3u) == static_cast<uint32_t>(player + 1) || ((seen >> k) & 1u);
+                    features(cw[k], player, shown, lo, hi);
+                };
                 uint32_t w[12];
 #pragma unroll
                 for (int pair = 0; pair < 4; ++pair) {
                     uint32_t lo0, hi0, lo1, hi1;
-                    cell_features(c0 + 2 * pair, cw[2 * pair], lo0, hi0);
-                    cell_features(c0 + 2 * pair + 1, cw[2 * pair + 1], lo1, hi1);
+                    group_features(2 * pair, lo0, hi0);
+                    group_features(2 * pair + 1, lo1, hi1);
                     w[3 * pair] = lo0;
                     w[3 * pair + 1] = hi0 | (lo1 << 16);
                     w[3 * pair + 2] = (lo1 >> 16) | (hi1 << 16);
